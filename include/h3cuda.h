@@ -1,0 +1,171 @@
+/*
+ * h3cuda.h -- C ABI of the B200 (sm_100a) H3 self-attention hot path.
+ *
+ * This is the boundary a Swift `CUDABackend: H3AttentionBackend` (module
+ * CH3Cuda) or any ctypes / cffi caller binds.  Plain pointers and sizes only;
+ * no C++ or torch types.  Every call returns an h3c_status and never aborts;
+ * h3c_last_error() gives the message of the last failure on a context.
+ *
+ * What each entry point replaces in the reference (MiniMax-H3-Swift):
+ *   h3c_attn_fwd          H3AttentionBackend.attend + AttentionLayer.sdpa
+ *                         (Sources/H3Attention/AttentionBackend.swift:126-127,
+ *                          Sources/H3Modules/DiTBlock.swift:293-328); with
+ *                         H3C_FUSE_PROLOGUE it also covers the per-head
+ *                         qNorm/kNorm and SplitHalfRoPE of
+ *                         AttentionLayer.callAsFunction (DiTBlock.swift:346-352)
+ *   h3c_prologue          H3RMSNorm (Sources/H3Modules/Modulation.swift:116-120)
+ *                         + SplitHalfRoPE.apply (DiTBlock.swift:83-103);
+ *                         the unfused bisection kernel
+ *   h3c_rope_table        H3RoPE.angles + rotationTable
+ *                         (Sources/H3Modules/H3Transformer.swift:62-78),
+ *                         built once per render in prepareRender (:263-276)
+ *   h3c_blockmask_build   new: the compacted 128x128 block list (no reference
+ *                         counterpart; prefix rule of AxialTopology.allows,
+ *                         Sources/H3Attention/AxialTopology.swift:128-137)
+ *   h3c_device_info       H3Hardware Machine.detect (Sources/H3Hardware/
+ *                         Machine.swift:48-56), for CUDA devices and NVLink
+ *   h3c_init/h3c_destroy  the backend instance AttentionRegistry.resolve
+ *                         creates once per render (AttentionBackend.swift:255-259)
+ */
+#ifndef H3CUDA_H
+#define H3CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define H3C_ABI_VERSION 1
+
+typedef enum h3c_status {
+  H3C_OK = 0,
+  H3C_ERR_INVALID_ARGUMENT = 1,   /* null pointer, negative size, bad stride */
+  H3C_ERR_UNSUPPORTED = 2,        /* geometry the kernels decline (e.g. head_dim != 128) */
+  H3C_ERR_CUDA = 3,               /* a CUDA runtime / driver call failed */
+  H3C_ERR_NCCL = 4,               /* reserved for the sequence-sharded path */
+  H3C_ERR_TIMEOUT = 5,            /* a bounded device wait gave up */
+  H3C_ERR_CAPACITY = 6,           /* caller buffer or fixed limit too small */
+  H3C_ERR_NO_DEVICE = 7           /* no sm_100 device, or the device is not usable */
+} h3c_status;
+
+typedef struct h3c_ctx h3c_ctx;
+
+/* Device discovery (the CUDA counterpart of H3Hardware.Machine). */
+typedef struct h3c_devinfo {
+  int32_t device;
+  int32_t cc_major, cc_minor;
+  int32_t sm_count;
+  int64_t hbm_bytes;
+  int64_t hbm_free_bytes;
+  int32_t max_smem_per_block_optin;
+  int32_t l2_bytes;
+  int32_t peer_count;         /* devices this one can access peer-to-peer */
+  int32_t nvlink_peer_mask;   /* bit d set: device d is a P2P peer */
+  char name[96];
+} h3c_devinfo;
+
+/* Block-mask specification (128x128 blocks in raster token order).
+ * Tokens [0, prefix_len) are the conditioning prefix (e.g. audio); tokens
+ * [prefix_len, seq_len) are a frames x height x width video lattice in t-major,
+ * h, w order.  Query block i (blocks touching the prefix keep every key
+ * block) keeps: every prefix key block; every video key block whose coarse
+ * cell (t/cell_t, h/cell_h, w/cell_w of the block's first token) lies within
+ * (radius_t, radius_h, radius_w) of its own; then n_random distinct extra key
+ * blocks drawn with splitmix64 from seed ^ (i * 0x9E3779B97F4A7C15). */
+typedef struct h3c_mask_spec {
+  int32_t seq_len, block, prefix_len;
+  int32_t frames, height, width;
+  int32_t cell_t, cell_h, cell_w;
+  int32_t radius_t, radius_h, radius_w;
+  int32_t n_random;
+  uint64_t seed;
+} h3c_mask_spec;
+
+/* A bf16 [tokens, heads, 128] operand: element (s, h, d) sits at
+ * ptr[s * token_stride + h * head_stride + d].  [S,H,D] has
+ * (token_stride, head_stride) = (H*D, D); the seam's [H,S,D] has (D, S*D). */
+typedef struct h3c_view {
+  void* ptr;
+  int64_t token_stride;
+  int64_t head_stride;
+} h3c_view;
+
+enum {
+  H3C_FUSE_PROLOGUE = 1,      /* q, k are pre-norm; apply RMSNorm + RoPE */
+  H3C_KERNEL_MMA_SYNC = 2,    /* force the mma.sync bisection kernel */
+  H3C_NO_ROPE = 4             /* with H3C_FUSE_PROLOGUE: RMSNorm only */
+};
+
+typedef struct h3c_attn_args {
+  h3c_view q, k, v, out;      /* bf16 device memory; out may not alias q/k/v */
+  int32_t seq_len;            /* S (valid tokens) */
+  int32_t heads;              /* heads present in the views */
+  int32_t head_dim;           /* must be 128 */
+  int32_t head_offset;        /* process heads [head_offset, head_offset+head_count) */
+  int32_t head_count;
+  float scale;                /* softmax scale, 1/sqrt(head_dim) in H3 */
+  const int32_t* row_ptr;     /* device CSR of the block mask: [n_blocks+1] */
+  const int32_t* col_idx;     /* device, ascending within each row */
+  int32_t block;              /* must be 128 */
+  int32_t flags;              /* H3C_* flags above */
+  /* prologue (read when H3C_FUSE_PROLOGUE is set) */
+  const void* q_norm_weight;  /* bf16 [128] */
+  const void* k_norm_weight;  /* bf16 [128] */
+  float eps;
+  const void* rope_table;     /* bf16 [S, rope_half, 4]: (c, -s, s, c) */
+  int32_t rope_half;          /* rotated pairs; 2*rope_half <= 128 */
+} h3c_attn_args;
+
+/* --- lifecycle --------------------------------------------------------- */
+int h3c_abi_version(void);
+h3c_status h3c_init(int device, h3c_ctx** out);
+h3c_status h3c_destroy(h3c_ctx* ctx);
+const char* h3c_last_error(const h3c_ctx* ctx);   /* never NULL */
+h3c_status h3c_device_info(h3c_ctx* ctx, h3c_devinfo* info);
+h3c_status h3c_device_count(int* count);
+
+/* --- block mask ---------------------------------------------------------- */
+/* Host builder.  row_ptr: [n_blocks+1] or NULL; col_idx: capacity entries or
+ * NULL (query nnz first).  n_blocks = ceil(seq_len / block). */
+h3c_status h3c_blockmask_build(const h3c_mask_spec* spec, int32_t* row_ptr, int32_t* col_idx,
+                               int64_t capacity, int64_t* nnz);
+/* Device builder, bit-identical to the host one.  d_row_ptr [n_blocks+1] and
+ * d_col_idx [capacity] are device memory; *nnz is written on the host after a
+ * stream synchronise.  Asynchronous otherwise. */
+h3c_status h3c_blockmask_build_device(h3c_ctx* ctx, const h3c_mask_spec* spec, int32_t* d_row_ptr,
+                                      int32_t* d_col_idx, int64_t capacity, int64_t* nnz,
+                                      void* stream);
+
+/* --- prologue and rope ---------------------------------------------------- */
+/* RoPE table on the device from integer positions d_pos [S,3] (t,h,w):
+ * dims = rotary channels per axis (sum = 2*half), theta as H3RoPE. */
+h3c_status h3c_rope_table(h3c_ctx* ctx, const int32_t* d_pos, int32_t seq_len, const int32_t dims[3],
+                          double theta, void* d_table, void* stream);
+/* out = SplitHalfRoPE(RMSNorm(x)) for one operand (q or k), rows (s, h) for
+ * h in [head_offset, head_offset+head_count).  table NULL: RMSNorm only. */
+h3c_status h3c_prologue(h3c_ctx* ctx, h3c_view x, h3c_view out, int32_t seq_len, int32_t heads,
+                        int32_t head_offset, int32_t head_count, const void* norm_weight, float eps,
+                        const void* rope_table, int32_t rope_half, void* stream);
+
+/* --- attention ------------------------------------------------------------ */
+/* Block-sparse attention forward, asynchronous on `stream` (a cudaStream_t,
+ * NULL = legacy default stream).  With H3C_FUSE_PROLOGUE the context's
+ * workspace holds the normalised keys (grown on demand with cudaMalloc). */
+h3c_status h3c_attn_fwd(h3c_ctx* ctx, const h3c_attn_args* args, void* stream);
+/* Bytes of workspace h3c_attn_fwd needs for these args. */
+h3c_status h3c_attn_workspace_size(const h3c_attn_args* args, size_t* bytes);
+/* Synchronous helper for tests: h3c_attn_fwd then a stream synchronise. */
+h3c_status h3c_attn_fwd_sync(h3c_ctx* ctx, const h3c_attn_args* args, void* stream);
+
+/* --- synthetic inputs ------------------------------------------------------ */
+/* Counter-based N(mean, std) bf16 generator; element i is a function of
+ * (seed, stream_id, i) only, bit-identical to the CPU checker's generator. */
+h3c_status h3c_fill_normal_bf16(h3c_ctx* ctx, void* d_out, int64_t n, uint64_t seed, uint64_t stream_id,
+                                double mean, double std, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* H3CUDA_H */

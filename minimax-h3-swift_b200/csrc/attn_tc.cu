@@ -1,0 +1,509 @@
+// Block-sparse attention forward on the Blackwell tensor cores (sm_100a):
+// tcgen05.mma with TMEM accumulators, TMA-staged K/V tiles, warp-specialised.
+//
+// Semantics: for every 128-row query block i and head h, one online softmax
+// over the kept key blocks of row i of the compacted block list, in ascending
+// order (Sources/H3Attention/AxialReference.swift:116-171 restated per block;
+// key columns past seq_len are masked).  Output bf16, O / max(l, 1e-30).
+//
+// CTA = one query block x two heads (the block list is shared by all heads,
+// so both tiles walk the same key blocks).  Roles:
+//   warp 0      TMA producer: Q tiles once, then K/V tiles into a 4-slot ring
+//   warp 1      MMA issuer (one elected thread): S = Q K^T (SS), O += P V (TS)
+//   warp 2      TMEM allocator (512 columns)
+//   warps 4-7   softmax + epilogue of tile 0 (thread = query row = TMEM lane)
+//   warps 8-11  softmax + epilogue of tile 1
+// TMEM columns: tile t owns [256t, 256t+128) for S (P is written back over its
+// first 64 columns as packed bf16) and [256t+128, 256t+256) for O.
+// Shared tiles are 128 rows x 64 bf16 (128 B) boxes in the 128-byte swizzle;
+// Q and K are K-major operands, V is an MN-major operand.
+//
+// Every mbarrier wait is bounded (wall-clock limit via %globaltimer).  On a
+// timeout the waiting thread records H3C_ERR_TIMEOUT in the status word,
+// raises a CTA-wide abort flag, and every role drains to the common exit,
+// where TMEM is freed.
+#include <cuda.h>
+
+#include "common.cuh"
+
+namespace h3 {
+namespace {
+
+constexpr int kThreads = 384;
+constexpr int kStages = 4;
+constexpr int kTileBytes = 128 * 128 * 2;   // one 128x128 bf16 tile
+constexpr int kHalfBytes = kTileBytes / 2;  // one 128x64 swizzle box
+constexpr uint64_t kWaitLimitNs = 4000000000ull;  // 4 s
+
+struct __align__(8) Barriers {
+  uint64_t q_full[2];
+  uint64_t kv_full[kStages];
+  uint64_t kv_empty[kStages];
+  uint64_t s_full[2];
+  uint64_t p_full[2];
+  uint64_t o_full[2];
+  uint32_t tmem_base;
+  int32_t abort;
+};
+
+constexpr int kSmemTiles = 2 * kTileBytes + kStages * kTileBytes;
+constexpr int kSmemBytes = kSmemTiles + 1024 /*align slack*/ + 256 /*barriers*/;
+
+// ------------------------------------------------------------- primitives
+__device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ uint64_t globaltimer() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count));
+}
+
+__device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait; false on abort/timeout.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int32_t* abort_flag,
+                                          int32_t* status) {
+  for (int i = 0; i < 64; ++i)
+    if (mbar_try(bar, parity)) return true;
+  const uint64_t t0 = globaltimer();
+  while (true) {
+    if (mbar_try(bar, parity)) return true;
+    if (*abort_flag) return false;
+    if (globaltimer() - t0 > kWaitLimitNs) {
+      *abort_flag = 1;
+      if (status) atomicExch(status, (int32_t)H3C_ERR_TIMEOUT);
+      return false;
+    }
+  }
+}
+
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+
+// 3D tiled TMA load (no multicast): coordinates (d, token, head).
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, uint32_t bar, int c0, int c1,
+                                            int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], "
+      "[%2];" ::"r"(dst),
+      "l"(map), "r"(bar), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tc_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+
+// D[tmem] (+)= A[smem desc] * B[smem desc]
+__device__ __forceinline__ void mma_ss(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d),
+      "l"(a), "l"(b), "r"(idesc), "r"(acc)
+      : "memory");
+}
+
+// D[tmem] (+)= A[tmem] * B[smem desc]
+__device__ __forceinline__ void mma_ts(uint32_t d, uint32_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d),
+      "r"(a), "l"(b), "r"(idesc), "r"(acc)
+      : "memory");
+}
+
+#define H3_TMEM_LD16(addr, r)                                                                                 \
+  asm volatile(                                                                                               \
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];" \
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),       \
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])  \
+      : "r"(addr))
+
+#define H3_TMEM_ST16(addr, r)                                                                                  \
+  asm volatile(                                                                                                \
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" \
+      ::"r"(addr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),       \
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])              \
+      : "memory")
+
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
+// Shared-memory matrix descriptor, 128-byte swizzle (layout type 2),
+// descriptor version 1; lbo/sbo in bytes.
+__device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = 0;
+  d |= (uint64_t)((addr >> 4) & 0x3FFF);
+  d |= (uint64_t)((lbo >> 4) & 0x3FFF) << 16;
+  d |= (uint64_t)((sbo >> 4) & 0x3FFF) << 32;
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)2 << 61;
+  return d;
+}
+
+// Instruction descriptor, kind::f16: bf16 x bf16 -> f32, M = 128, N = 128.
+constexpr uint32_t idesc_bf16(bool b_mn_major) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((b_mn_major ? 1u : 0u) << 16) | ((128u >> 3) << 17) |
+         ((128u >> 4) << 24);
+}
+
+// ------------------------------------------------------------------ kernel
+__global__ void __launch_bounds__(kThreads, 1)
+    attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                   const __grid_constant__ CUtensorMap tm_v, AttnLaunch a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  uint8_t* sQ = smem;                        // 2 tiles
+  uint8_t* sKV = smem + 2 * kTileBytes;      // kStages tiles
+  Barriers* bars = (Barriers*)(smem + kSmemTiles);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int qb = blockIdx.x;
+  const int h0 = blockIdx.y * 2;
+  const int ntile = (h0 + 1 < a.head_count) ? 2 : 1;
+  const int p0 = a.row_ptr[qb];
+  const int nkv = a.row_ptr[qb + 1] - p0;
+  volatile int32_t* abort_flag = &bars->abort;
+
+  if (threadIdx.x == 0) {
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(smem_u32(&bars->q_full[t]), 1);
+      mbar_init(smem_u32(&bars->s_full[t]), 1);
+      mbar_init(smem_u32(&bars->p_full[t]), 128);
+      mbar_init(smem_u32(&bars->o_full[t]), 1);
+    }
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(smem_u32(&bars->kv_full[s]), 1);
+      mbar_init(smem_u32(&bars->kv_empty[s]), 1);
+    }
+    bars->abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 2) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(
+                     smem_u32(&bars->tmem_base)));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = bars->tmem_base;
+
+  if (nkv > 0) {
+    if (warp == 0) {
+      // ------------------------------------------------------- TMA producer
+      if (lane == 0) {
+        for (int t = 0; t < ntile; ++t) {
+          uint32_t bar = smem_u32(&bars->q_full[t]);
+          mbar_expect_tx(bar, kTileBytes);
+          uint32_t dst = smem_u32(sQ + t * kTileBytes);
+          tma_load_3d(dst, &tm_q, bar, 0, qb * 128, h0 + t);
+          tma_load_3d(dst + kHalfBytes, &tm_q, bar, 64, qb * 128, h0 + t);
+        }
+        int n = 0;
+        bool ok = true;
+        // consumption order: K_t(0) for each tile, then per j and tile: V_t(j), K_t(j+1)
+        auto load = [&](const CUtensorMap* map, int jb, int head) {
+          const int slot = n % kStages;
+          const uint32_t ph = (uint32_t)((n / kStages) & 1);
+          if (!mbar_wait(smem_u32(&bars->kv_empty[slot]), ph ^ 1u, abort_flag, a.status)) {
+            ok = false;
+            return;
+          }
+          uint32_t bar = smem_u32(&bars->kv_full[slot]);
+          mbar_expect_tx(bar, kTileBytes);
+          uint32_t dst = smem_u32(sKV + slot * kTileBytes);
+          tma_load_3d(dst, map, bar, 0, jb * 128, head);
+          tma_load_3d(dst + kHalfBytes, map, bar, 64, jb * 128, head);
+          ++n;
+        };
+        for (int t = 0; t < ntile && ok; ++t) load(&tm_k, a.col_idx[p0], h0 + t);
+        for (int j = 0; j < nkv && ok; ++j) {
+          for (int t = 0; t < ntile && ok; ++t) {
+            load(&tm_v, a.col_idx[p0 + j], h0 + t);
+            if (ok && j + 1 < nkv) load(&tm_k, a.col_idx[p0 + j + 1], h0 + t);
+          }
+        }
+        // Drain: wait for the last loads to land before anyone may exit.
+        if (!ok) {
+          for (int m = (n > kStages ? n - kStages : 0); m < n; ++m) {
+            const int slot = m % kStages;
+            const uint32_t ph = (uint32_t)((m / kStages) & 1);
+            volatile int32_t zero = 0;
+            mbar_wait(smem_u32(&bars->kv_full[slot]), ph, &zero, nullptr);
+          }
+        }
+      }
+    } else if (warp == 1) {
+      // ------------------------------------------------------------ MMA issuer
+      if (lane == 0) {
+        constexpr uint32_t kIdS = idesc_bf16(false);
+        constexpr uint32_t kIdPV = idesc_bf16(true);
+        bool ok = true;
+        for (int t = 0; t < ntile && ok; ++t) ok = mbar_wait(smem_u32(&bars->q_full[t]), 0, abort_flag, a.status);
+        tc_fence_after();
+        int n = 0;
+        auto wait_slot = [&](int& slot) -> bool {
+          slot = n % kStages;
+          const uint32_t ph = (uint32_t)((n / kStages) & 1);
+          if (!mbar_wait(smem_u32(&bars->kv_full[slot]), ph, abort_flag, a.status)) return false;
+          tc_fence_after();
+          return true;
+        };
+        auto issue_s = [&](int t) -> bool {  // S_t = Q_t K^T
+          int slot;
+          if (!wait_slot(slot)) return false;
+          const uint32_t qa = smem_u32(sQ + t * kTileBytes);
+          const uint32_t kbase = smem_u32(sKV + slot * kTileBytes);
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk) {
+            const uint32_t off = (kk >> 2) * kHalfBytes + (kk & 3) * 32;
+            mma_ss(tmem + 256 * t, smem_desc(qa + off, 16, 1024), smem_desc(kbase + off, 16, 1024), kIdS,
+                   kk > 0 ? 1u : 0u);
+          }
+          tc_commit(smem_u32(&bars->kv_empty[slot]));
+          ++n;
+          return true;
+        };
+        auto issue_pv = [&](int t, int j) -> bool {  // O_t += P_t V
+          int slot;
+          if (!wait_slot(slot)) return false;
+          const uint32_t vbase = smem_u32(sKV + slot * kTileBytes);
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk) {
+            mma_ts(tmem + 256 * t + 128, tmem + 256 * t + kk * 8, smem_desc(vbase + kk * 2048, kHalfBytes, 1024),
+                   kIdPV, (j > 0 || kk > 0) ? 1u : 0u);
+          }
+          tc_commit(smem_u32(&bars->kv_empty[slot]));
+          ++n;
+          return true;
+        };
+        for (int t = 0; t < ntile && ok; ++t) {
+          ok = issue_s(t);
+          if (ok) tc_commit(smem_u32(&bars->s_full[t]));
+        }
+        for (int j = 0; j < nkv && ok; ++j) {
+          for (int t = 0; t < ntile && ok; ++t) {
+            ok = mbar_wait(smem_u32(&bars->p_full[t]), (uint32_t)(j & 1), abort_flag, a.status);
+            if (!ok) break;
+            tc_fence_after();
+            ok = issue_pv(t, j);
+            if (!ok) break;
+            if (j + 1 < nkv) {
+              ok = issue_s(t);
+              if (ok) tc_commit(smem_u32(&bars->s_full[t]));
+            } else {
+              tc_commit(smem_u32(&bars->o_full[t]));
+            }
+          }
+        }
+        if (!ok) {  // let every issued MMA retire before TMEM is released
+          tc_commit(smem_u32(&bars->o_full[0]));
+        }
+      }
+    } else if (warp >= 4) {
+      // --------------------------------------------------- softmax + epilogue
+      const int t = (warp - 4) >> 2;
+      const int q = warp & 3;  // TMEM lane quarter this warp may access
+      if (t < ntile) {
+        const uint32_t lane_base = (uint32_t)(32 * q) << 16;
+        const uint32_t tS = tmem + lane_base + 256 * t;
+        const uint32_t tO = tS + 128;
+        const float sl2 = a.scale_log2;
+        float m = -1e30f, l = 0.f;
+        bool ok = true;
+        for (int j = 0; j < nkv; ++j) {
+          if (!mbar_wait(smem_u32(&bars->s_full[t]), (uint32_t)(j & 1), abort_flag, a.status)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          uint32_t s[128];
+#pragma unroll
+          for (int c = 0; c < 8; ++c) H3_TMEM_LD16(tS + 16 * c, (&s[16 * c]));
+          tmem_wait_ld();
+          const int valid = a.seq_len - a.col_idx[p0 + j] * 128;
+          if (valid < 128) {
+#pragma unroll
+            for (int c = 0; c < 128; ++c)
+              if (c >= valid) s[c] = __float_as_uint(-INFINITY);
+          }
+          float mx = -INFINITY;
+#pragma unroll
+          for (int c = 0; c < 128; ++c) mx = fmaxf(mx, __uint_as_float(s[c]));
+          const float mxs = mx * sl2;
+          // Lazy rescale: keep the running max unless the new one exceeds it
+          // by more than 8 (a factor 256 in the exponentials).
+          bool need = (j == 0) ? false : (mxs > m + 8.0f);
+          if (j == 0) m = mxs;
+          if (__any_sync(0xffffffff, need)) {
+            const float f = need ? ex2(m - mxs) : 1.0f;
+            if (need) {
+              l *= f;
+              m = mxs;
+            }
+#pragma unroll
+            for (int c = 0; c < 8; ++c) {
+              uint32_t o[16];
+              H3_TMEM_LD16(tO + 16 * c, o);
+              tmem_wait_ld();
+#pragma unroll
+              for (int e = 0; e < 16; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * f);
+              H3_TMEM_ST16(tO + 16 * c, o);
+            }
+          }
+          float sum = 0.f;
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            uint32_t pk[16];
+#pragma unroll
+            for (int e = 0; e < 16; ++e) {
+              float p0v = ex2(fmaf(__uint_as_float(s[32 * c + 2 * e]), sl2, -m));
+              float p1v = ex2(fmaf(__uint_as_float(s[32 * c + 2 * e + 1]), sl2, -m));
+              sum += p0v + p1v;
+              pk[e] = pack_bf16(p0v, p1v);
+            }
+            H3_TMEM_ST16(tS + 16 * c, pk);
+          }
+          l += sum;
+          tmem_wait_st();
+          tc_fence_before();
+          mbar_arrive(smem_u32(&bars->p_full[t]));
+        }
+        if (ok && mbar_wait(smem_u32(&bars->o_full[t]), 0, abort_flag, a.status)) {
+          tc_fence_after();
+          const int row = qb * 128 + 32 * q + lane;
+          const float inv = 1.0f / fmaxf(l, 1e-30f);
+          uint16_t* go = a.o + (int64_t)(h0 + t) * a.o_head + (int64_t)row * a.o_tok;
+#pragma unroll
+          for (int c = 0; c < 8; ++c) {
+            uint32_t o[16];
+            H3_TMEM_LD16(tO + 16 * c, o);
+            tmem_wait_ld();
+            uint4 w0, w1;
+            w0.x = pack_bf16(__uint_as_float(o[0]) * inv, __uint_as_float(o[1]) * inv);
+            w0.y = pack_bf16(__uint_as_float(o[2]) * inv, __uint_as_float(o[3]) * inv);
+            w0.z = pack_bf16(__uint_as_float(o[4]) * inv, __uint_as_float(o[5]) * inv);
+            w0.w = pack_bf16(__uint_as_float(o[6]) * inv, __uint_as_float(o[7]) * inv);
+            w1.x = pack_bf16(__uint_as_float(o[8]) * inv, __uint_as_float(o[9]) * inv);
+            w1.y = pack_bf16(__uint_as_float(o[10]) * inv, __uint_as_float(o[11]) * inv);
+            w1.z = pack_bf16(__uint_as_float(o[12]) * inv, __uint_as_float(o[13]) * inv);
+            w1.w = pack_bf16(__uint_as_float(o[14]) * inv, __uint_as_float(o[15]) * inv);
+            if (row < a.seq_len) {
+              reinterpret_cast<uint4*>(go + 16 * c)[0] = w0;
+              reinterpret_cast<uint4*>(go + 16 * c)[1] = w1;
+            }
+          }
+        }
+      }
+    }
+  }
+
+  // ------------------------------------------------------------------ exit
+  tc_fence_before();
+  __syncthreads();
+  if (bars->abort) {
+    // an aborted MMA warp committed to o_full[0]; wait (bounded) for it so
+    // that no MMA is still writing TMEM when it is released
+    volatile int32_t zero = 0;
+    if (warp == 2) mbar_wait(smem_u32(&bars->o_full[0]), 0, &zero, nullptr);
+    __syncwarp();
+  }
+  if (warp == 2) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tmem));
+  }
+}
+
+// --------------------------------------------------------------- host side
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn get_encode() {
+  static EncodeTiledFn fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = (EncodeTiledFn)p;
+  }
+  return fn;
+}
+
+// (d, token, head) view of a strided bf16 operand, boxes of 64 x 128 x 1.
+bool make_map(CUtensorMap* m, const void* base, int64_t tok_stride, int64_t head_stride, int seq, int heads,
+              std::string* err) {
+  EncodeTiledFn enc = get_encode();
+  if (!enc) {
+    if (err) *err = "cuTensorMapEncodeTiled unavailable; ";
+    return false;
+  }
+  cuuint64_t dims[3] = {128, (cuuint64_t)seq, (cuuint64_t)heads};
+  cuuint64_t strides[2] = {(cuuint64_t)tok_stride * 2, (cuuint64_t)head_stride * 2};
+  cuuint32_t box[3] = {64, 128, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    if (err) *err = "cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + "); ";
+    return false;
+  }
+  return true;
+}
+
+}  // namespace
+
+cudaError_t launch_attn_tc(const AttnLaunch& a, cudaStream_t s, std::string* err) {
+  CUtensorMap mq, mk, mv;
+  if (!make_map(&mq, a.q, a.q_tok, a.q_head, a.seq_len, a.head_count, err) ||
+      !make_map(&mk, a.k, a.k_tok, a.k_head, a.seq_len, a.head_count, err) ||
+      !make_map(&mv, a.v, a.v_tok, a.v_head, a.seq_len, a.head_count, err))
+    return cudaErrorInvalidValue;
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaError_t e = cudaFuncSetAttribute(attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+    if (e != cudaSuccess) return e;
+    attr_set = true;
+  }
+  dim3 grid(a.n_blocks, (a.head_count + 1) / 2);
+  attn_tc_kernel<<<grid, kThreads, kSmemBytes, s>>>(mq, mk, mv, a);
+  return cudaGetLastError();
+}
+
+}  // namespace h3

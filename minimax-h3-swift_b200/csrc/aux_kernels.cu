@@ -1,0 +1,264 @@
+// Small kernels around the attention: the Q/K prologue (RMSNorm + split-half
+// RoPE), the RoPE table, the block-mask builder and the synthetic-input
+// generator.  All are HBM- or latency-bound; the attention kernels are where
+// the time goes.
+#include "common.cuh"
+
+namespace h3 {
+namespace {
+
+// ---------------------------------------------------------------- prologue
+// One warp per (token, head) row of 128 channels; lane l owns channels
+// l, l+32, l+64, l+96 (coalesced 64-byte accesses per instruction).
+// RMSNorm follows Sources/H3Modules/Modulation.swift:116-120 (fp32 sum of
+// squares, fp32 products, bf16 result); the rotation follows
+// Sources/H3Modules/DiTBlock.swift:83-103 with each product and sum rounded
+// to bf16 as in Tests/H3ModulesTests/QKFusionMetalFixture.swift:57-69.
+__global__ void prologue_kernel(const uint16_t* __restrict__ x, int64_t x_tok, int64_t x_head,
+                                uint16_t* __restrict__ y, int64_t y_tok, int64_t y_head, int32_t seq_len,
+                                int32_t head_count, const uint16_t* __restrict__ w, float eps,
+                                const uint16_t* __restrict__ table, int32_t half) {
+  __shared__ float rowbuf[8][128];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * 8 + warp;
+  if (row >= (int64_t)seq_len * head_count) return;
+  const int64_t s = row / head_count, h = row % head_count;
+  const uint16_t* xr = x + s * x_tok + h * x_head;
+  float v[4];
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    v[i] = bf2f(xr[lane + 32 * i]);
+    ss += v[i] * v[i];
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffff, ss, o);
+  const float inv = 1.0f / sqrtf(ss / 128.f + eps);
+  float* rb = rowbuf[warp];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    int d = lane + 32 * i;
+    rb[d] = rbf((v[i] * inv) * bf2f(w[d]));
+  }
+  __syncwarp();
+  uint16_t* yr = y + s * y_tok + h * y_head;
+  const uint16_t* t = table ? table + s * (int64_t)half * 4 : nullptr;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    int d = lane + 32 * i;
+    float out = rb[d];
+    if (t && d < 2 * half) {
+      if (d < half) {
+        float c = bf2f(t[4 * d]), ns = bf2f(t[4 * d + 1]);
+        out = rbf(rbf(c * rb[d]) + rbf(ns * rb[d + half]));
+      } else {
+        int p = d - half;
+        float sn = bf2f(t[4 * p + 2]), c2 = bf2f(t[4 * p + 3]);
+        out = rbf(rbf(sn * rb[p]) + rbf(c2 * rb[d]));
+      }
+    }
+    yr[d] = f2bf(out);
+  }
+}
+
+// -------------------------------------------------------------- rope table
+// Follows H3RoPE.angles / rotationTable (Sources/H3Modules/H3Transformer.swift:62-78):
+// fp32 inv_freq, fp32 angle = pos * inv, cos/sin evaluated in double on the
+// fp32 angle and rounded to fp32 then bf16; entry = (c, -s, s, c).
+__global__ void rope_table_kernel(const int32_t* __restrict__ pos, int32_t seq_len, int3 dims,
+                                  const float* __restrict__ inv, int32_t half, uint16_t* __restrict__ table) {
+  int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= (int64_t)seq_len * half) return;
+  int64_t s = idx / half;
+  int i = (int)(idx % half);
+  int axis = i < dims.x / 2 ? 0 : (i < (dims.x + dims.y) / 2 ? 1 : 2);
+  float p = (float)pos[s * 3 + axis];
+  float ang = __fmul_rn(p, inv[i]);
+  float c = (float)cos((double)ang), sn = (float)sin((double)ang);
+  uint16_t* t = table + idx * 4;
+  t[0] = f2bf(c);
+  t[1] = f2bf(-sn);
+  t[2] = f2bf(sn);
+  t[3] = f2bf(c);
+}
+
+// ------------------------------------------------------------- block mask
+// One CTA per query block: a shared bitmap of kept key blocks, then the
+// ascending column list.  Pass 0 writes row counts; pass 1 (after a
+// single-CTA exclusive scan) writes col_idx.  Rule identical to the host
+// builder in api.cu.
+struct MaskDev {
+  int32_t seq_len, block, prefix_len, frames, height, width, cell_t, cell_h, cell_w, radius_t, radius_h,
+      radius_w, n_random;
+  uint64_t seed;
+  int32_t nb, npb;
+};
+
+__device__ __forceinline__ void cell_of(const MaskDev& m, int b, int& ct, int& ch, int& cw) {
+  int64_t v = (int64_t)b * m.block - m.prefix_len;
+  int64_t per = (int64_t)m.height * m.width;
+  int t = (int)(v / per), rem = (int)(v % per);
+  ct = t / m.cell_t;
+  ch = (rem / m.width) / m.cell_h;
+  cw = (rem % m.width) / m.cell_w;
+}
+
+__global__ void mask_rows_kernel(MaskDev m, int32_t* __restrict__ counts, const int32_t* __restrict__ row_ptr,
+                                 int32_t* __restrict__ col_idx, int64_t capacity, int pass) {
+  extern __shared__ uint32_t bits[];
+  const int i = blockIdx.x;
+  const int words = (m.nb + 31) / 32;
+  const bool dense = i < m.npb;
+  for (int wd = threadIdx.x; wd < words; wd += blockDim.x) bits[wd] = 0;
+  __syncthreads();
+  if (dense) {
+    for (int j = threadIdx.x; j < m.nb; j += blockDim.x) atomicOr(&bits[j >> 5], 1u << (j & 31));
+  } else {
+    int qt, qh, qw;
+    cell_of(m, i, qt, qh, qw);
+    for (int j = threadIdx.x; j < m.nb; j += blockDim.x) {
+      bool keep = j < m.npb;
+      if (!keep) {
+        int kt, kh, kw;
+        cell_of(m, j, kt, kh, kw);
+        keep = abs(kt - qt) <= m.radius_t && abs(kh - qh) <= m.radius_h && abs(kw - qw) <= m.radius_w;
+      }
+      if (keep) atomicOr(&bits[j >> 5], 1u << (j & 31));
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {  // the draws are sequential by definition
+      uint64_t state = m.seed ^ ((uint64_t)i * 0x9E3779B97F4A7C15ull);
+      int added = 0, draws = 64 + 16 * m.n_random;
+      for (int a = 0; a < draws && added < m.n_random; ++a) {
+        state = splitmix64(state);
+        int j = (int)(((state >> 32) * (uint64_t)m.nb) >> 32);
+        if (!(bits[j >> 5] & (1u << (j & 31)))) {
+          bits[j >> 5] |= 1u << (j & 31);
+          ++added;
+        }
+      }
+    }
+  }
+  __syncthreads();
+  if (pass == 0) {
+    __shared__ int total;
+    if (threadIdx.x == 0) total = 0;
+    __syncthreads();
+    int c = 0;
+    for (int wd = threadIdx.x; wd < words; wd += blockDim.x) c += __popc(bits[wd]);
+    atomicAdd(&total, c);
+    __syncthreads();
+    if (threadIdx.x == 0) counts[i] = total;
+    return;
+  }
+  // pass 1: thread 0 walks the bitmap in order (nb <= a few thousand)
+  if (threadIdx.x == 0) {
+    int64_t off = row_ptr[i];
+    for (int wd = 0; wd < words; ++wd) {
+      uint32_t b = bits[wd];
+      while (b) {
+        int j = wd * 32 + __ffs(b) - 1;
+        b &= b - 1;
+        if (off < capacity) col_idx[off] = j;
+        ++off;
+      }
+    }
+  }
+}
+
+__global__ void scan_kernel(const int32_t* __restrict__ counts, int32_t nb, int32_t* __restrict__ row_ptr,
+                            int64_t* __restrict__ nnz) {
+  // single CTA, sequential chunks: nb is at most tens of thousands
+  __shared__ int64_t part[1024];
+  const int t = threadIdx.x, n = blockDim.x;
+  const int chunk = (nb + n - 1) / n;
+  int64_t sum = 0;
+  for (int i = t * chunk; i < min(nb, (t + 1) * chunk); ++i) sum += counts[i];
+  part[t] = sum;
+  __syncthreads();
+  if (t == 0) {
+    int64_t run = 0;
+    for (int i = 0; i < n; ++i) {
+      int64_t v = part[i];
+      part[i] = run;
+      run += v;
+    }
+    *nnz = run;
+  }
+  __syncthreads();
+  int64_t run = part[t];
+  for (int i = t * chunk; i < min(nb, (t + 1) * chunk); ++i) {
+    row_ptr[i] = (int32_t)run;
+    run += counts[i];
+  }
+  if (t * chunk < nb && (t + 1) * chunk >= nb) row_ptr[nb] = (int32_t)run;  // the last non-empty chunk
+  if (nb == 0 && t == 0) row_ptr[0] = 0;
+}
+
+// ---------------------------------------------------------- synthetic data
+__global__ void fill_normal_kernel(uint16_t* __restrict__ out, int64_t n, uint64_t seed, uint64_t stream,
+                                   double mean, double std) {
+  const uint64_t key = splitmix64(seed ^ (stream * 0xD1B54A32D192ED03ull));
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    uint64_t hsh = splitmix64(key + ((uint64_t)i >> 1));
+    double u1 = ((double)(hsh >> 40) + 1.0) * (1.0 / 16777216.0);
+    double u2 = (double)(hsh & 0xFFFFFFull) * (1.0 / 16777216.0);
+    double r = sqrt(-2.0 * log(u1));
+    double ang = 6.283185307179586 * u2;
+    double z = (i & 1) ? r * sin(ang) : r * cos(ang);
+    out[i] = f2bf((float)(mean + std * z));
+  }
+}
+
+}  // namespace
+
+cudaError_t launch_prologue(const uint16_t* x, int64_t x_tok, int64_t x_head, uint16_t* y, int64_t y_tok,
+                            int64_t y_head, int32_t seq_len, int32_t head_count, const uint16_t* w, float eps,
+                            const uint16_t* table, int32_t half, cudaStream_t s) {
+  int64_t rows = (int64_t)seq_len * head_count;
+  if (rows == 0) return cudaSuccess;
+  prologue_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, s>>>(x, x_tok, x_head, y, y_tok, y_head, seq_len,
+                                                             head_count, w, eps, table, half);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_rope_table(const int32_t* pos, int32_t seq_len, int3 dims, const float* d_inv, int32_t half,
+                              uint16_t* table, cudaStream_t s) {
+  int64_t n = (int64_t)seq_len * half;
+  if (n == 0) return cudaSuccess;
+  rope_table_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(pos, seq_len, dims, d_inv, half, table);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_mask_build(const h3c_mask_spec& sp, int32_t* counts, int32_t* row_ptr, int32_t* col_idx,
+                              int64_t capacity, int64_t* d_nnz, cudaStream_t s) {
+  MaskDev m;
+  m.seq_len = sp.seq_len; m.block = sp.block; m.prefix_len = sp.prefix_len;
+  m.frames = sp.frames; m.height = sp.height; m.width = sp.width;
+  m.cell_t = sp.cell_t; m.cell_h = sp.cell_h; m.cell_w = sp.cell_w;
+  m.radius_t = sp.radius_t; m.radius_h = sp.radius_h; m.radius_w = sp.radius_w;
+  m.n_random = sp.n_random; m.seed = sp.seed;
+  m.nb = (sp.seq_len + sp.block - 1) / sp.block;
+  m.npb = (sp.prefix_len + sp.block - 1) / sp.block;
+  size_t smem = (size_t)((m.nb + 31) / 32) * 4;
+  if (smem > 48 * 1024) return cudaErrorInvalidValue;
+  mask_rows_kernel<<<m.nb, 256, smem, s>>>(m, counts, nullptr, nullptr, 0, 0);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  scan_kernel<<<1, 1024, 0, s>>>(counts, m.nb, row_ptr, d_nnz);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  mask_rows_kernel<<<m.nb, 256, smem, s>>>(m, nullptr, row_ptr, col_idx, capacity, 1);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_fill_normal(uint16_t* out, int64_t n, uint64_t seed, uint64_t stream, double mean, double std,
+                               int sm_count, cudaStream_t s) {
+  if (n == 0) return cudaSuccess;
+  int64_t blocks = (n + 255) / 256;
+  int64_t cap = (int64_t)sm_count * 16;
+  fill_normal_kernel<<<(unsigned)(blocks < cap ? blocks : cap), 256, 0, s>>>(out, n, seed, stream, mean, std);
+  return cudaGetLastError();
+}
+
+}  // namespace h3

@@ -1,0 +1,86 @@
+// Shared helpers of the H3 attention library (sm_100a only).
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <string>
+
+#include "h3cuda.h"
+
+struct h3c_ctx {
+  int device = 0;
+  std::string err;
+  cudaDeviceProp prop{};
+  void* workspace = nullptr;      // normalised keys/queries of the fused path
+  size_t workspace_bytes = 0;
+  int64_t* d_counter = nullptr;   // small device scratch (mask builder nnz)
+};
+
+namespace h3 {
+
+constexpr int kHeadDim = 128;
+constexpr int kBlock = 128;
+
+__host__ __device__ inline uint64_t splitmix64(uint64_t x) {
+  x += 0x9E3779B97F4A7C15ull;
+  x = (x ^ (x >> 30)) * 0xBF58476D1CE4E5B9ull;
+  x = (x ^ (x >> 27)) * 0x94D049BB133111EBull;
+  return x ^ (x >> 31);
+}
+
+__device__ __forceinline__ float bf2f(uint16_t h) { return __uint_as_float((uint32_t)h << 16); }
+
+// round-to-nearest-even; identical to the CPU checker's conversion
+__device__ __forceinline__ uint16_t f2bf(float f) {
+  uint32_t u = __float_as_uint(f);
+  if ((u & 0x7fffffffu) > 0x7f800000u) return (uint16_t)((u >> 16) | 0x40);
+  u += 0x7fffu + ((u >> 16) & 1u);
+  return (uint16_t)(u >> 16);
+}
+
+__device__ __forceinline__ float rbf(float f) { return bf2f(f2bf(f)); }
+
+// The RMSNorm + split-half RoPE of one 128-wide row held as x[0..127] (fp32
+// values of bf16 inputs) by one thread: y = bf16(x * rsqrt(mean(x^2)+eps) * w),
+// then ra = bf16(bf16(c*a) + bf16(-s*b)), rb = bf16(bf16(s*a) + bf16(c*b)).
+// Used by the fused tcgen05 Q path; the standalone prologue kernel computes
+// the same arithmetic with a warp per row.
+
+}  // namespace h3
+
+#define H3_CUDA_TRY(ctx, expr)                                                   \
+  do {                                                                           \
+    cudaError_t e_ = (expr);                                                     \
+    if (e_ != cudaSuccess) {                                                     \
+      if (ctx) (ctx)->err = std::string(#expr) + ": " + cudaGetErrorString(e_);  \
+      return H3C_ERR_CUDA;                                                       \
+    }                                                                            \
+  } while (0)
+
+// Launchers implemented in the kernel translation units.
+namespace h3 {
+
+struct AttnLaunch {
+  // operands (bf16), element strides
+  const uint16_t* q; int64_t q_tok, q_head;
+  const uint16_t* k; int64_t k_tok, k_head;
+  const uint16_t* v; int64_t v_tok, v_head;
+  uint16_t* o; int64_t o_tok, o_head;
+  int32_t seq_len, n_blocks, head_count;
+  float scale_log2;               // scale * log2(e)
+  const int32_t* row_ptr;
+  const int32_t* col_idx;
+  // fused Q prologue (tcgen05 path only); q_norm == nullptr means q is final
+  const uint16_t* q_norm; const uint16_t* rope; int32_t rope_half; float eps;
+  int32_t* status;                // device status word (bounded waits), may be null
+};
+
+cudaError_t launch_attn_mma(const AttnLaunch& a, cudaStream_t s);
+cudaError_t launch_attn_tc(const AttnLaunch& a, cudaStream_t s, std::string* err);
+cudaError_t launch_prologue(const uint16_t* x, int64_t x_tok, int64_t x_head, uint16_t* y, int64_t y_tok,
+                            int64_t y_head, int32_t seq_len, int32_t head_count, const uint16_t* w,
+                            float eps, const uint16_t* table, int32_t half, cudaStream_t s);
+
+}  // namespace h3

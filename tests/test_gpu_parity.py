@@ -1,0 +1,218 @@
+"""CUDA path vs the CPU checker, through the C ABI (B200 only).
+
+Tolerances: integer and generator work is bit-exact; the prologue is within
+one bf16 ulp (reduction order of the fp32 sum of squares; the reference's own
+bound is relRMS < 1e-3 and worst < 8 ulp, QKFusionTests.swift:109-110);
+attention on unit-variance inputs is max-abs <= 2e-2 and mean-abs <= 2e-3
+against the fp32 restatement.
+"""
+import numpy as np
+import pytest
+
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+MAX_ABS, MEAN_ABS = 2e-2, 2e-3
+
+
+def _t(a, dev):
+    import torch
+
+    return torch.from_numpy(a.view(np.int16)).view(torch.bfloat16).to(dev)
+
+
+def _np(t):
+    import torch
+
+    return t.detach().cpu().contiguous().view(torch.int16).numpy().view(np.uint16)
+
+
+def _rt():
+    from h3attention import Runtime
+
+    return Runtime.get(0)
+
+
+def _spec(**kw):
+    from h3attention import MaskSpec
+
+    return MaskSpec(**kw)
+
+
+def _check_attn(got_bf16_shd, want_hsd, rows=None):
+    got = O.bf16_to_f32(got_bf16_shd).transpose(1, 0, 2)
+    if rows is not None:
+        got, want_hsd = got[:, rows], want_hsd[:, rows]
+    err = np.abs(got - want_hsd)
+    assert np.isfinite(got).all()
+    assert err.max() <= MAX_ABS, f"max-abs {err.max()}"
+    assert err.mean() <= MEAN_ABS, f"mean-abs {err.mean()}"
+    return float(err.max()), float(err.mean())
+
+
+# --------------------------------------------------------------- aux kernels
+def test_fill_normal_matches_checker(gpu):
+    import torch
+
+    out = torch.empty(1 << 20, dtype=torch.bfloat16, device=gpu)
+    _rt().fill_normal(out, 1234, 3)
+    torch.cuda.synchronize()
+    ref = O.fill_normal_bf16((1 << 20,), 1234, 3)
+    assert np.count_nonzero(_np(out) != ref) <= 2
+
+
+def test_rope_table_matches_checker(gpu):
+    import torch
+
+    from h3attention.configs import CONFIGS
+
+    pos = CONFIGS["config1"].positions()
+    tab = _rt().rope_table(torch.from_numpy(pos).to(gpu))
+    ref = O.rope_table(pos)
+    diff = np.abs(_np(tab).astype(np.int32) - ref.astype(np.int32))
+    assert diff.max() <= 1 and np.count_nonzero(diff) <= 4
+
+
+@pytest.mark.parametrize("S,H,half", [(4096, 8, 64), (1000, 3, 48), (257, 2, 0)])
+def test_prologue_matches_checker(gpu, S, H, half):
+    import torch
+
+    x = O.fill_normal_bf16((S, H, 128), 21, 1)
+    w = O.fill_normal_bf16((128,), 21, 4, 1.0, 0.02)
+    if half:
+        dims = (32, 48, 48) if half == 64 else (32, 32, 32)
+        pos = np.stack([np.arange(S) % 17, np.arange(S) % 13, np.arange(S) % 11], 1).astype(np.int32)
+        tab = O.rope_table(pos, dims=dims)
+    else:
+        tab = None
+    ref = O.prologue(x, w, 1e-6, tab)
+    xd = _t(x, gpu)
+    out = torch.empty_like(xd)
+    _rt().prologue(xd, out, _t(w, gpu), 1e-6, None if tab is None else _t(tab, gpu))
+    torch.cuda.synchronize()
+    got = _np(out)
+    g, r = O.bf16_to_f32(got), O.bf16_to_f32(ref)
+    if tab is None:  # RMSNorm alone: one rounding of a correctly ordered product
+        assert np.abs(got.astype(np.int32) - ref.astype(np.int32)).max() <= 1
+    # the reference's gate (QKFusionTests.swift:67-110): relRMS < 1e-3 and a
+    # worst error, scaled by |ref| + rms, under 8 bf16 ulp (2^-7 each)
+    rms = np.sqrt(np.mean(r ** 2))
+    assert np.sqrt(np.mean((g - r) ** 2)) / rms < 1e-3
+    assert np.max(np.abs(g - r) / (np.abs(r) + rms)) / 0.0078125 < 8
+
+
+MASKS = [
+    dict(seq_len=4096, frames=16, height=16, width=16, n_random=2, seed=1),
+    dict(seq_len=125632, prefix_len=640, frames=31, height=48, width=84, radius_h=2, radius_w=2, n_random=4, seed=3),
+    dict(seq_len=800, prefix_len=100, frames=7, height=10, width=10, n_random=50, seed=5),
+]
+
+
+@pytest.mark.parametrize("kw", MASKS)
+def test_device_blockmask_bit_identical(gpu, kw):
+    rp, ci = _rt().blockmask_device(_spec(**kw), capacity=400000)
+    wrp, wci = O.blockmask_build(O.mask_spec(**kw))
+    assert np.array_equal(rp.cpu().numpy(), wrp) and np.array_equal(ci.cpu().numpy(), wci)
+
+
+# ----------------------------------------------------------------- attention
+def _case(S, H, spec_kw, seed=4):
+    q, k, v = (O.fill_normal_bf16((S, H, 128), seed, st) for st in (1, 2, 3))
+    rp, ci = O.blockmask_build(O.mask_spec(**spec_kw))
+    return q, k, v, rp, ci
+
+
+ATTN_CASES = {
+    "config1": (4096, 8, dict(seq_len=4096, frames=16, height=16, width=16, n_random=2, seed=1)),
+    "ragged_odd_heads": (1000, 3, dict(seq_len=1000, frames=10, height=10, width=10, n_random=1, seed=2)),
+    "prefix": (1640, 2, dict(seq_len=1640, prefix_len=640, frames=10, height=10, width=10, n_random=1, seed=3)),
+    "one_block": (77, 1, dict(seq_len=77, frames=7, height=1, width=11)),
+    "dense_ragged": (1500, 2, dict(seq_len=1500, prefix_len=1500, frames=0, height=0, width=0)),
+}
+
+
+@pytest.mark.parametrize("kernel", ["mma_sync", "tcgen05"])
+@pytest.mark.parametrize("name", list(ATTN_CASES))
+def test_attention_matches_checker(gpu, kernel, name):
+    import torch
+
+    from h3attention import _lib
+
+    S, H, kw = ATTN_CASES[name]
+    q, k, v, rp, ci = _case(S, H, kw)
+    want = O.attend_streaming(q, k, v, rp, ci)
+    qd, kd, vd = (_t(a, gpu) for a in (q, k, v))
+    out = torch.full_like(qd, float("nan"))
+    blocks = (torch.from_numpy(rp).to(gpu), torch.from_numpy(ci).to(gpu))
+    flags = _lib.H3C_KERNEL_MMA_SYNC if kernel == "mma_sync" else 0
+    _rt().attn_fwd(q=qd, k=kd, v=vd, out=out, layout="SHD", scale=1 / np.sqrt(128), blocks=blocks, flags=flags)
+    torch.cuda.synchronize()
+    _check_attn(_np(out), want)
+
+
+@pytest.mark.parametrize("kernel", ["mma_sync", "tcgen05"])
+def test_fused_prologue_matches_checker(gpu, kernel):
+    import torch
+
+    from h3attention import _lib
+    from h3attention.configs import CONFIGS
+
+    wl = CONFIGS["config1"]
+    S, H = wl.seq_len, wl.heads
+    q, k, v = (O.fill_normal_bf16((S, H, 128), 9, st) for st in (1, 2, 3))
+    wq, wk = (O.fill_normal_bf16((128,), 9, st, 1.0, 0.02) for st in (4, 5))
+    tab = O.rope_table(wl.positions())
+    rp, ci = O.blockmask_build(O.mask_spec(seq_len=S, frames=16, height=16, width=16, n_random=2, seed=wl.seed))
+    want = O.attend_streaming(O.prologue(q, wq, 1e-6, tab), O.prologue(k, wk, 1e-6, tab), v, rp, ci)
+    qd, kd, vd = (_t(a, gpu) for a in (q, k, v))
+    out = torch.empty_like(qd)
+    blocks = (torch.from_numpy(rp).to(gpu), torch.from_numpy(ci).to(gpu))
+    flags = _lib.H3C_KERNEL_MMA_SYNC if kernel == "mma_sync" else 0
+    _rt().attn_fwd(q=qd, k=kd, v=vd, out=out, layout="SHD", scale=1 / np.sqrt(128), blocks=blocks, flags=flags,
+                   q_norm=_t(wq, gpu), k_norm=_t(wk, gpu), eps=1e-6, rope_table=_t(tab, gpu))
+    torch.cuda.synchronize()
+    _check_attn(_np(out), want)
+
+
+def test_hsd_layout_and_head_shard(gpu):
+    """The seam's [H,S,D] layout, and a head shard [1, 3) of 4 heads."""
+    import torch
+
+    S, H = 600, 4
+    q, k, v, rp, ci = _case(S, H, dict(seq_len=600, frames=6, height=10, width=10, n_random=1, seed=8))
+    want = O.attend_streaming(q, k, v, rp, ci)
+    qd, kd, vd = (_t(np.ascontiguousarray(a.transpose(1, 0, 2)), gpu) for a in (q, k, v))
+    out = torch.zeros_like(qd)
+    blocks = (torch.from_numpy(rp).to(gpu), torch.from_numpy(ci).to(gpu))
+    _rt().attn_fwd(q=qd, k=kd, v=vd, out=out, layout="HSD", scale=1 / np.sqrt(128), blocks=blocks, head_offset=1,
+                   head_count=2)
+    torch.cuda.synchronize()
+    got = _np(out.transpose(0, 1))
+    _check_attn(got[:, 1:3], want[1:3])
+    assert np.all(_np(out)[[0, 3]] == 0), "heads outside the shard are untouched"
+
+
+def test_full_size_config2_sampled(gpu):
+    """Config 2 at full size (S=124,992, H=40) on the tcgen05 kernel, checked
+    on a deterministic sample of query blocks and heads."""
+    import torch
+
+    from h3attention import BlockList, Runtime
+    from h3attention.configs import CONFIGS
+
+    wl = CONFIGS["config2"]
+    S, H = wl.seq_len, wl.heads
+    rt = Runtime.get(0)
+    q, k, v = (rt.fill_normal(torch.empty((S, H, 128), dtype=torch.bfloat16, device=gpu), wl.seed, st)
+               for st in (1, 2, 3))
+    bl = BlockList.build(wl.mask_spec())
+    out = torch.empty_like(q)
+    rt.attn_fwd(q=q, k=k, v=v, out=out, layout="SHD", scale=1 / np.sqrt(128), blocks=bl.on(gpu))
+    torch.cuda.synchronize()
+    qbs = [0, 1, 488, 975, 976]
+    heads = (17, 19)
+    qh, kh, vh = (_np(t[:, heads[0]:heads[1]]) for t in (q, k, v))
+    want = O.attend_streaming(qh, kh, vh, bl.row_ptr, bl.col_idx, qblocks=qbs)
+    rows = np.concatenate([np.arange(b * 128, min(S, b * 128 + 128)) for b in qbs])
+    _check_attn(_np(out[:, heads[0]:heads[1]]), want, rows=rows)
