@@ -1,0 +1,349 @@
+"""Benchmark of the H3 block-sparse attention hot path on B200.
+
+One step = one pass of the path on one synthetic batch: Q/K RMSNorm + 3D RoPE
+prologue and block-sparse attention over the compacted block list, through
+the C ABI (h3c_attn_fwd with H3C_FUSE_PROLOGUE).  Metric: effective TFLOP/s
+over kept blocks (4*H*D*sum of valid rows x cols of kept block pairs) and
+ms per call.  Inputs are bf16 N(0,1) from the seeded device generator and
+larger than L2 (no flush needed).
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--config config2]
+  python bench.py --impl reference ...   # the CPU restatement on host cores
+
+Multi-GPU (torchrun, one rank per GPU): every rank runs its own full call
+(weak scaling, no data-path collective); time = max over ranks.
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+for _p in (ROOT, os.path.join(ROOT, "minimax-h3-swift_b200")):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+METRIC = "effective TFLOP/s, H3 block-sparse attention (fused Q/K RMSNorm + 3D RoPE), per call"
+PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def _peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return p, "measured"
+    except OSError:
+        return PEAKS_FALLBACK, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi samples of SM clock and throttle reasons during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: int):
+        self.device, self.rows, self.proc = device, [], None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.device), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) == 8:
+                self.rows.append(parts)
+
+    def __exit__(self, *exc):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        if not self.rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        mhz = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in self.rows for i in range(4) if r[4 + i] == "Active"})
+        return {"sm_mhz": statistics.median(mhz) if mhz else None,
+                "sm_max_mhz": float(self.rows[0][2]) if self.rows[0][2].replace(".", "").isdigit() else None,
+                "reasons": reasons, "samples": len(self.rows)}
+
+
+def _dist():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return ws, rank, local
+
+
+def _workload(name, heads=None):
+    from h3attention.configs import CONFIGS, config5
+
+    from dataclasses import replace
+
+    wl = config5(float(name.split("@")[1])) if name.startswith("config5@") else CONFIGS[name]
+    if heads:
+        wl = replace(wl, heads=heads, name=f"{wl.name}/h{heads}")
+    return wl
+
+
+class CpuBaseline:
+    """The CPU restatement (oracle/, kind "port": the reference's Swift/MLX
+    path cannot run on Linux) timed on this host: prologue + streaming
+    attention over a deterministic sample of query blocks of the benchmark's
+    block list, every host core, extrapolated by counted kept-pair FLOPs."""
+
+    def __init__(self, wl, cores=None):
+        import numpy as np
+
+        from h3attention import BlockList
+        from oracle import oracle as O
+
+        self.O, self.np, self.wl = O, np, wl
+        L = O.lib()
+        if cores:
+            L.h3o_set_num_threads(cores)
+        self.threads = L.h3o_num_threads()
+        self.bl = BlockList.build(wl.mask_spec())
+        self.H = min(wl.heads, 2)
+        S, H = wl.seq_len, self.H
+        self.order = np.random.default_rng(7).permutation(self.bl.n_blocks)
+        self.sizes = np.minimum(128, S - np.arange(self.bl.n_blocks) * 128).astype(np.float64)
+        self.tab = O.rope_table(wl.positions())
+        self.q, self.k, self.v = (O.fill_normal_bf16((S, H, 128), wl.seed, st) for st in (1, 2, 3))
+        self.wq, self.wk = (O.fill_normal_bf16((128,), wl.seed, st, 1.0, 0.02) for st in (4, 5))
+        self.cursor = 0
+
+    def sample(self, budget_s):
+        O, np, bl, wl, H = self.O, self.np, self.bl, self.wl, self.H
+        t0 = time.perf_counter()
+        qn, kn = O.prologue(self.q, self.wq, 1e-6, self.tab), O.prologue(self.k, self.wk, 1e-6, self.tab)
+        pro_s = time.perf_counter() - t0
+        nb = bl.n_blocks
+        step = max(self.threads, 8)
+        done_flops, elapsed, used = 0.0, 0.0, 0
+        while elapsed < budget_s and used < nb:
+            idx = [(self.cursor + i) % nb for i in range(step)]
+            self.cursor = (self.cursor + step) % nb
+            qbs = self.order[idx]
+            used += len(qbs)
+            t0 = time.perf_counter()
+            O.attend_streaming(qn, kn, self.v, bl.row_ptr, bl.col_idx, qblocks=qbs)
+            elapsed += time.perf_counter() - t0
+            for b in qbs:
+                row = bl.col_idx[bl.row_ptr[b]:bl.row_ptr[b + 1]]
+                done_flops += 4.0 * H * 128 * self.sizes[b] * float(np.sum(self.sizes[row]))
+        pro_full = pro_s * wl.heads / H          # prologue of every head
+        attn_full = elapsed * bl.flops(wl.heads) / done_flops
+        ms = (pro_full + attn_full) * 1e3
+        return {"value": bl.flops(wl.heads) / (ms * 1e-3) / 1e12, "unit": "TFLOP/s", "cores": self.threads,
+                "kind": "port", "ms_per_call": ms,
+                "sample": f"{used} of {nb} query blocks x {H} of {wl.heads} heads ({elapsed:.1f} s attention, "
+                          f"{pro_s:.1f} s prologue of {H} heads), extrapolated by kept-pair FLOPs"}
+
+
+def run_reference(args):
+    ws, rank, _ = _dist()
+    if rank != 0:
+        return 0
+    wl = _workload(args.config, args.heads)
+    from h3attention import BlockList
+
+    bl = BlockList.build(wl.mask_spec())
+    base = CpuBaseline(wl)
+    budget = max(2.0, args.ref_budget / (args.warmup + args.steps))
+    vals, cb = [], None
+    for i in range(args.warmup + args.steps):
+        cb = base.sample(budget)
+        if i >= args.warmup:
+            vals.append(cb["value"])
+    v = statistics.median(vals)
+    ms = bl.flops(wl.heads) / (v * 1e12) * 1e3
+    line = {"metric": METRIC, "value": v, "unit": "TFLOP/s", "n_gpus": ws, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "impl": "reference",
+            "config": {"workload": wl.name, "seq_len": wl.seq_len, "heads": wl.heads, "head_dim": 128,
+                       "density": bl.density},
+            "cpu_baseline": {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")},
+            "e2e": {"value": v, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# Per-launch DRAM traffic of attn_tc_kernel on config2 (dram__bytes_read.sum +
+# dram__bytes_write.sum), from the ncu capture summarised in
+# profiles/attn_tc_kernel_config2.md; None until that capture exists.
+TRAFFIC_BYTES = {}
+
+
+def _timed(fn, steps):
+    import torch
+
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / steps
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    from h3attention import BlockList, Runtime
+    from h3attention.configs import EPS, ROPE_DIMS, ROPE_THETA, STREAM_K, STREAM_Q, STREAM_V, STREAM_WK, STREAM_WQ
+
+    ws, rank, local = _dist()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if ws > 1:
+        dist.init_process_group("nccl", device_id=dev)
+    wl = _workload(args.config, args.heads)
+    S, H = wl.seq_len, wl.heads
+    rt = Runtime.get(local)
+    bf = torch.bfloat16
+
+    def fill(shape, stream, mean=0.0, std=1.0):
+        return rt.fill_normal(torch.empty(shape, dtype=bf, device=dev), wl.seed + rank, stream, mean, std)
+
+    q, k, v = fill((S, H, 128), STREAM_Q), fill((S, H, 128), STREAM_K), fill((S, H, 128), STREAM_V)
+    wq, wk = fill((128,), STREAM_WQ, 1.0, 0.02), fill((128,), STREAM_WK, 1.0, 0.02)
+    tab = rt.rope_table(torch.from_numpy(wl.positions()).to(dev), ROPE_DIMS, ROPE_THETA)
+    bl = BlockList.build(wl.mask_spec())
+    blocks = bl.on(dev)
+    flops = bl.flops(H)
+    out = torch.empty_like(q)
+    scale = 128 ** -0.5
+    fused = rt.attn_args(q, k, v, out, "SHD", scale, blocks, q_norm=wq, k_norm=wk, eps=EPS, rope_table=tab)
+
+    def step():
+        rt.attn_fwd_args(fused)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if ws > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        ms = _timed(step, args.steps)
+    if ws > 1:
+        dist.barrier()
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    value = ws * flops / (ms * 1e-3) / 1e12
+    launches = 3 * args.steps  # K prologue, Q prologue, attention per call
+
+    # Roofline pass: the attention kernel alone on pre-normalised Q/K, each
+    # launch bracketed by events on the launching stream.
+    qn, kn = torch.empty_like(q), torch.empty_like(k)
+    rt.prologue(q, qn, wq, EPS, tab)
+    rt.prologue(k, kn, wk, EPS, tab)
+    plain = rt.attn_args(qn, kn, v, out, "SHD", scale, blocks)
+    for _ in range(2):
+        rt.attn_fwd_args(plain)
+    times = []
+    for _ in range(args.steps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        rt.attn_fwd_args(plain)
+        e1.record()
+        times.append((e0, e1))
+    torch.cuda.synchronize()
+    attn_ms = statistics.mean(a.elapsed_time(b) for a, b in times)
+    del qn, kn
+
+    # End to end through the public call with host buffers: pinned host
+    # q/k/v -> device, the fused call, result -> pinned host, every step.
+    hq, hk, hv = (t.cpu().pin_memory() for t in (q, k, v))
+    hout = torch.empty(out.shape, dtype=bf).pin_memory()
+
+    def e2e_step():
+        q.copy_(hq, non_blocking=True)
+        k.copy_(hk, non_blocking=True)
+        v.copy_(hv, non_blocking=True)
+        rt.attn_fwd_args(fused)
+        hout.copy_(out, non_blocking=True)
+
+    e2e_step()
+    torch.cuda.synchronize()
+    e2e_ms = _timed(e2e_step, max(2, min(args.steps, 5)))
+    if ws > 1:
+        t = torch.tensor([e2e_ms, attn_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms, attn_ms = (float(x) for x in t.tolist())
+    h2d = 3 * q.numel() * 2
+    d2h = out.numel() * 2
+
+    if rank == 0:
+        peaks, src = _peaks()
+        achieved = flops / (attn_ms * 1e-3) / 1e12
+        traffic = TRAFFIC_BYTES.get(wl.name)
+        line = {
+            "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": ws, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1) bf16; shapes of the workload)",
+            "config": {"workload": wl.name, "seq_len": S, "heads": H, "head_dim": 128, "block": 128,
+                       "density": round(bl.density, 4), "kept_blocks": bl.nnz, "flops_per_call": flops,
+                       "l2": "inputs larger than L2 (no flush)", "parallelism": f"replicas x{ws} (weak)",
+                       "prologue": "fused RMSNorm + RoPE (t/h/w 32/48/48, theta 1e4)"},
+            "e2e": {"value": ws * flops / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": e2e_ms,
+                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+            "roofline": {"bound": "tensor", "kernel": "attn_tc_kernel", "achieved": achieved,
+                         "peak": peaks["bf16_tflops"], "unit": "TFLOP/s", "frac": achieved / peaks["bf16_tflops"],
+                         "frac_sustained": achieved / peaks["bf16_tflops_sustained"], "peak_source": src,
+                         "kernel_ms": attn_ms, "traffic": traffic},
+            "gpu_launches": launches,
+            "clocks": clk.summary(),
+        }
+        if ws == 1 and not args.no_cpu_baseline:
+            cb = CpuBaseline(wl).sample(args.cpu_budget)
+            line["cpu_baseline"] = {k2: cb[k2] for k2 in ("value", "unit", "cores", "kind", "sample")}
+        print(json.dumps(line), flush=True)
+    if ws > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--config", default="config2",
+                    help="config1..config4 or config5@<density>; default config2 (the 5 s 1344x768 clip)")
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--cpu-budget", type=float, default=15.0, help="seconds of CPU baseline sampling")
+    ap.add_argument("--ref-budget", type=float, default=120.0, help="total seconds for --impl reference")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--heads", type=int, default=None,
+                    help="override the workload's head count (small profiling cases only)")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+    return run_reference(args) if args.impl == "reference" else run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -105,6 +105,8 @@ h3c_status check_attn(h3c_ctx* ctx, const h3c_attn_args* a) {
         return fail(ctx, H3C_ERR_UNSUPPORTED, "h3c_attn_fwd: rope_half must be in [1, 64]");
     }
     if (!(a->eps >= 0.f)) return fail(ctx, H3C_ERR_INVALID_ARGUMENT, "h3c_attn_fwd: eps must be >= 0");
+    if (((uintptr_t)a->q_norm_weight & 15) || ((uintptr_t)a->k_norm_weight & 15) || ((uintptr_t)a->rope_table & 7))
+      return fail(ctx, H3C_ERR_UNSUPPORTED, "h3c_attn_fwd: norm weights need 16-byte, the rope table 8-byte alignment");
   }
   // 16-byte aligned rows are required by the vectorised and TMA loads.
   const h3c_view* vs[4] = {&a->q, &a->k, &a->v, &a->out};
@@ -284,6 +286,10 @@ h3c_status h3c_prologue(h3c_ctx* ctx, h3c_view x, h3c_view out, int32_t seq_len,
     return fail(ctx, H3C_ERR_INVALID_ARGUMENT, "h3c_prologue: invalid argument");
   if (rope_table && (rope_half <= 0 || 2 * rope_half > 128))
     return fail(ctx, H3C_ERR_UNSUPPORTED, "h3c_prologue: rope_half must be in [1, 64]");
+  if (((uintptr_t)x.ptr & 15) || ((uintptr_t)out.ptr & 15) || (x.token_stride & 7) || (x.head_stride & 7) ||
+      (out.token_stride & 7) || (out.head_stride & 7) || ((uintptr_t)norm_weight & 15) ||
+      ((uintptr_t)rope_table & 7))
+    return fail(ctx, H3C_ERR_UNSUPPORTED, "h3c_prologue: rows, weight and table need 16/16/8-byte alignment");
   H3_CUDA_TRY(ctx, cudaSetDevice(ctx->device));
   const uint16_t* xp = (const uint16_t*)x.ptr + (int64_t)head_offset * x.head_stride;
   uint16_t* yp = (uint16_t*)out.ptr + (int64_t)head_offset * out.head_stride;

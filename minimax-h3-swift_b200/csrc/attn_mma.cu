@@ -226,11 +226,16 @@ __global__ void __launch_bounds__(kThreads, 1) attn_mma_kernel(AttnLaunch a) {
 
 cudaError_t launch_attn_mma(const AttnLaunch& a, cudaStream_t s) {
   const int smem = kRows * 256 + 4 * kTileKeys * 256;
-  static bool attr_set = false;
-  if (!attr_set) {
+  // function attributes are per device context: remember them per device
+  static bool attr_set[64] = {};
+  int dev = 0;
+  cudaError_t de = cudaGetDevice(&dev);
+  if (de != cudaSuccess) return de;
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  if (!attr_set[dev]) {
     cudaError_t e = cudaFuncSetAttribute(attn_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
-    attr_set = true;
+    attr_set[dev] = true;
   }
   dim3 grid(a.n_blocks, a.head_count);
   attn_mma_kernel<<<grid, kThreads, smem, s>>>(a);

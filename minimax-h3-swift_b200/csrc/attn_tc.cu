@@ -24,6 +24,8 @@
 // where TMEM is freed.
 #include <cuda.h>
 
+#include <cstdlib>
+
 #include "common.cuh"
 
 namespace h3 {
@@ -157,6 +159,53 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
+// 2^x on the FMA pipe, for the share of the exponentials that would
+// otherwise queue on the MUFU unit.  Cody-Waite split x = n + f with
+// n = round(x) (via the 1.5*2^23 rounding constant) and f in [-0.5, 0.5];
+// 2^f by a cubic fitted here for minimum relative error on that interval
+// (max relative error 7.6e-5, far below the bf16 rounding P receives);
+// 2^n is added to the exponent field.  x is clamped at -126 so that the
+// result stays a non-negative finite number (masked entries give ~1e-38).
+__device__ __forceinline__ float ex2_poly(float x) {
+  constexpr float kC0 = 0.99992817640304565f, kC1 = 0.69326096773147583f, kC2 = 0.24260970950126648f,
+                  kC3 = 0.055170975625514984f;
+  constexpr float kRound = 12582912.0f;
+  x = fmaxf(x, -126.0f);
+  const float t = __fadd_rn(x, kRound);
+  const float f = __fsub_rn(x, __fsub_rn(t, kRound));
+  const float p = fmaf(fmaf(fmaf(kC3, f, kC2), f, kC1), f, kC0);
+  return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
+}
+
+__device__ __forceinline__ float max3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
+// (x0, x1) = (s0, s1) * k + b on the packed f32x2 pipe; k, b hold a scalar
+// in both halves.
+__device__ __forceinline__ void fma2(float& x0, float& x1, uint32_t s0, uint32_t s1, uint64_t k, uint64_t b) {
+  asm("{\n\t.reg .b64 a, d;\n\tmov.b64 a, {%2, %3};\n\t"
+      "fma.rn.ftz.f32x2 d, a, %4, %5;\n\tmov.b64 {%0, %1}, d;\n\t}"
+      : "=f"(x0), "=f"(x1)
+      : "r"(s0), "r"(s1), "l"(k), "l"(b));
+}
+
+__device__ __forceinline__ uint64_t add2(uint64_t acc, float a, float b) {
+  uint64_t r;
+  asm("{\n\t.reg .b64 t;\n\tmov.b64 t, {%2, %3};\n\tadd.rn.ftz.f32x2 %0, %1, t;\n\t}"
+      : "=l"(r)
+      : "l"(acc), "f"(a), "f"(b));
+  return r;
+}
+
+__device__ __forceinline__ uint64_t dup2(float v) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %1};" : "=l"(r) : "f"(v));
+  return r;
+}
+
 __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&v);
@@ -181,6 +230,7 @@ constexpr uint32_t idesc_bf16(bool b_mn_major) {
 }
 
 // ------------------------------------------------------------------ kernel
+template <int EMU>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                    const __grid_constant__ CUtensorMap tm_v, AttnLaunch a) {
@@ -221,8 +271,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = bars->tmem_base;
+  // Register split: the launch gives 384 x 168; the producer/MMA warpgroup
+  // keeps 56 and the two softmax warpgroups take 224 each
+  // (4*32*56 + 8*32*224 = 64512 = 384*168; the host checks the launch count).
 
-  if (nkv > 0) {
+  if (warp < 4) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 56;");
+   if (nkv > 0) {
     if (warp == 0) {
       // ------------------------------------------------------- TMA producer
       if (lane == 0) {
@@ -334,7 +389,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           tc_commit(smem_u32(&bars->o_full[0]));
         }
       }
-    } else if (warp >= 4) {
+    }
+   }
+  } else {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 224;");
+   if (nkv > 0) {
+    {
       // --------------------------------------------------- softmax + epilogue
       const int t = (warp - 4) >> 2;
       const int q = warp & 3;  // TMEM lane quarter this warp may access
@@ -345,6 +405,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         const float sl2 = a.scale_log2;
         float m = -1e30f, l = 0.f;
         bool ok = true;
+        // only the sequence's last block can be partial, and it can only be
+        // the last kept block of this row (the list is ascending)
+        const int last_valid = a.seq_len - a.col_idx[p0 + nkv - 1] * 128;
+        const uint64_t sl2x2 = dup2(sl2);
         for (int j = 0; j < nkv; ++j) {
           if (!mbar_wait(smem_u32(&bars->s_full[t]), (uint32_t)(j & 1), abort_flag, a.status)) {
             ok = false;
@@ -355,15 +419,22 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int c = 0; c < 8; ++c) H3_TMEM_LD16(tS + 16 * c, (&s[16 * c]));
           tmem_wait_ld();
-          const int valid = a.seq_len - a.col_idx[p0 + j] * 128;
+          const int valid = (j == nkv - 1) ? last_valid : 128;
           if (valid < 128) {
 #pragma unroll
             for (int c = 0; c < 128; ++c)
               if (c >= valid) s[c] = __float_as_uint(-INFINITY);
           }
-          float mx = -INFINITY;
+          float mxa[4];
 #pragma unroll
-          for (int c = 0; c < 128; ++c) mx = fmaxf(mx, __uint_as_float(s[c]));
+          for (int g = 0; g < 4; ++g) {
+            float r = __uint_as_float(s[32 * g]);
+#pragma unroll
+            for (int c = 1; c < 31; c += 2)
+              r = max3(r, __uint_as_float(s[32 * g + c]), __uint_as_float(s[32 * g + c + 1]));
+            mxa[g] = fmaxf(r, __uint_as_float(s[32 * g + 31]));
+          }
+          const float mx = max3(mxa[0], mxa[1], fmaxf(mxa[2], mxa[3]));
           const float mxs = mx * sl2;
           // Lazy rescale: keep the running max unless the new one exceeds it
           // by more than 8 (a factor 256 in the exponentials).
@@ -385,20 +456,29 @@ __global__ void __launch_bounds__(kThreads, 1)
               H3_TMEM_ST16(tO + 16 * c, o);
             }
           }
-          float sum = 0.f;
+          const uint64_t negm = dup2(-m);
+          uint64_t sum2 = 0;
 #pragma unroll
           for (int c = 0; c < 4; ++c) {
             uint32_t pk[16];
 #pragma unroll
             for (int e = 0; e < 16; ++e) {
-              float p0v = ex2(fmaf(__uint_as_float(s[32 * c + 2 * e]), sl2, -m));
-              float p1v = ex2(fmaf(__uint_as_float(s[32 * c + 2 * e + 1]), sl2, -m));
-              sum += p0v + p1v;
+              float x0, x1;
+              fma2(x0, x1, s[32 * c + 2 * e], s[32 * c + 2 * e + 1], sl2x2, negm);
+              float p0v, p1v;
+              if ((e & 7) < EMU) {
+                p0v = ex2_poly(x0);
+                p1v = ex2_poly(x1);
+              } else {
+                p0v = ex2(x0);
+                p1v = ex2(x1);
+              }
+              sum2 = add2(sum2, p0v, p1v);
               pk[e] = pack_bf16(p0v, p1v);
             }
             H3_TMEM_ST16(tS + 16 * c, pk);
           }
-          l += sum;
+          l += __uint_as_float((uint32_t)sum2) + __uint_as_float((uint32_t)(sum2 >> 32));
           tmem_wait_st();
           tc_fence_before();
           mbar_arrive(smem_u32(&bars->p_full[t]));
@@ -430,6 +510,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
+   }
   }
 
   // ------------------------------------------------------------------ exit
@@ -487,6 +568,33 @@ bool make_map(CUtensorMap* m, const void* base, int64_t tok_stride, int64_t head
   return true;
 }
 
+constexpr int kDefaultEmu = 0;
+
+template <int EMU>
+cudaError_t launch_variant(dim3 grid, cudaStream_t s, const CUtensorMap& mq, const CUtensorMap& mk,
+                           const CUtensorMap& mv, const AttnLaunch& a) {
+  // function attributes are per device context: remember them per device
+  static bool attr_set[64] = {};
+  int dev = 0;
+  cudaError_t de = cudaGetDevice(&dev);
+  if (de != cudaSuccess) return de;
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  if (!attr_set[dev]) {
+    cudaError_t e =
+        cudaFuncSetAttribute(attn_tc_kernel<EMU>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+    if (e != cudaSuccess) return e;
+    // setmaxnreg draws on the registers the block was launched with; the
+    // kernel's split needs exactly 168 per thread at launch.
+    cudaFuncAttributes fa;
+    e = cudaFuncGetAttributes(&fa, attn_tc_kernel<EMU>);
+    if (e != cudaSuccess) return e;
+    if (fa.numRegs != 168) return cudaErrorInvalidConfiguration;
+    attr_set[dev] = true;
+  }
+  attn_tc_kernel<EMU><<<grid, kThreads, kSmemBytes, s>>>(mq, mk, mv, a);
+  return cudaGetLastError();
+}
+
 }  // namespace
 
 cudaError_t launch_attn_tc(const AttnLaunch& a, cudaStream_t s, std::string* err) {
@@ -495,15 +603,24 @@ cudaError_t launch_attn_tc(const AttnLaunch& a, cudaStream_t s, std::string* err
       !make_map(&mk, a.k, a.k_tok, a.k_head, a.seq_len, a.head_count, err) ||
       !make_map(&mv, a.v, a.v_tok, a.v_head, a.seq_len, a.head_count, err))
     return cudaErrorInvalidValue;
-  static bool attr_set = false;
-  if (!attr_set) {
-    cudaError_t e = cudaFuncSetAttribute(attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
-    if (e != cudaSuccess) return e;
-    attr_set = true;
+  // Share of exponentials computed on the FMA pipe, in eighths (tuning knob
+  // H3C_EXP_EMU, read once; default chosen by measurement).
+  static int emu = -1;
+  if (emu < 0) {
+    const char* env = getenv("H3C_EXP_EMU");
+    emu = env ? atoi(env) : kDefaultEmu;
+    if (emu < 0 || emu > 8) emu = kDefaultEmu;
   }
   dim3 grid(a.n_blocks, (a.head_count + 1) / 2);
-  attn_tc_kernel<<<grid, kThreads, kSmemBytes, s>>>(mq, mk, mv, a);
-  return cudaGetLastError();
+  switch (emu) {
+    case 0: return launch_variant<0>(grid, s, mq, mk, mv, a);
+    case 2: return launch_variant<2>(grid, s, mq, mk, mv, a);
+    case 3: return launch_variant<3>(grid, s, mq, mk, mv, a);
+    case 4: return launch_variant<4>(grid, s, mq, mk, mv, a);
+    case 5: return launch_variant<5>(grid, s, mq, mk, mv, a);
+    case 6: return launch_variant<6>(grid, s, mq, mk, mv, a);
+    default: return launch_variant<kDefaultEmu>(grid, s, mq, mk, mv, a);
+  }
 }
 
 }  // namespace h3

@@ -8,57 +8,142 @@ namespace h3 {
 namespace {
 
 // ---------------------------------------------------------------- prologue
-// One warp per (token, head) row of 128 channels; lane l owns channels
-// l, l+32, l+64, l+96 (coalesced 64-byte accesses per instruction).
-// RMSNorm follows Sources/H3Modules/Modulation.swift:116-120 (fp32 sum of
-// squares, fp32 products, bf16 result); the rotation follows
+// 16 threads per (token, head) row of 128 channels, 8 contiguous channels
+// (one 16-byte load) per thread, 16 rows per 256-thread CTA.  RMSNorm follows
+// Sources/H3Modules/Modulation.swift:116-120 (fp32 sum of squares, fp32
+// products, bf16 result); the rotation follows
 // Sources/H3Modules/DiTBlock.swift:83-103 with each product and sum rounded
-// to bf16 as in Tests/H3ModulesTests/QKFusionMetalFixture.swift:57-69.
-__global__ void prologue_kernel(const uint16_t* __restrict__ x, int64_t x_tok, int64_t x_head,
-                                uint16_t* __restrict__ y, int64_t y_tok, int64_t y_head, int32_t seq_len,
-                                int32_t head_count, const uint16_t* __restrict__ w, float eps,
-                                const uint16_t* __restrict__ table, int32_t half) {
-  __shared__ float rowbuf[8][128];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t row = (int64_t)blockIdx.x * 8 + warp;
-  if (row >= (int64_t)seq_len * head_count) return;
-  const int64_t s = row / head_count, h = row % head_count;
-  const uint16_t* xr = x + s * x_tok + h * x_head;
-  float v[4];
+// to bf16 as in Tests/H3ModulesTests/QKFusionMetalFixture.swift:57-69.  The
+// normalised row is staged in shared memory because the rotation pairs
+// channel i with i + half for any half <= 64.
+__global__ void __launch_bounds__(256) prologue_kernel(const uint16_t* __restrict__ x, int64_t x_tok,
+                                                       int64_t x_head, uint16_t* __restrict__ y, int64_t y_tok,
+                                                       int64_t y_head, int32_t seq_len, int32_t head_count,
+                                                       const uint16_t* __restrict__ w, float eps,
+                                                       const uint16_t* __restrict__ table, int32_t half) {
+  __shared__ float rowbuf[16][129];
+  const int sub = threadIdx.x >> 4, t = threadIdx.x & 15;
+  const int64_t row = (int64_t)blockIdx.x * 16 + sub;
+  const bool live = row < (int64_t)seq_len * head_count;
+  const int64_t s = live ? row / head_count : 0, h = live ? row % head_count : 0;
+  float v[8];
   float ss = 0.f;
+  if (live) {
+    const uint4 raw = *reinterpret_cast<const uint4*>(x + s * x_tok + h * x_head + 8 * t);
+    const uint32_t wv[4] = {raw.x, raw.y, raw.z, raw.w};
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    v[i] = bf2f(xr[lane + 32 * i]);
-    ss += v[i] * v[i];
+    for (int i = 0; i < 4; ++i) {
+      v[2 * i] = __uint_as_float(wv[i] << 16);
+      v[2 * i + 1] = __uint_as_float(wv[i] & 0xffff0000u);
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) ss += v[i] * v[i];
   }
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffff, ss, o);
+  for (int o = 8; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffff, ss, o);
   const float inv = 1.0f / sqrtf(ss / 128.f + eps);
-  float* rb = rowbuf[warp];
+  const uint4 wraw = *reinterpret_cast<const uint4*>(w + 8 * t);
+  const uint32_t ww[4] = {wraw.x, wraw.y, wraw.z, wraw.w};
+  float* rb = rowbuf[sub];
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    int d = lane + 32 * i;
-    rb[d] = rbf((v[i] * inv) * bf2f(w[d]));
+  for (int i = 0; i < 8; ++i) {
+    const float wi = __uint_as_float(i & 1 ? (ww[i >> 1] & 0xffff0000u) : (ww[i >> 1] << 16));
+    rb[8 * t + i] = rbf((v[i] * inv) * wi);
   }
   __syncwarp();
-  uint16_t* yr = y + s * y_tok + h * y_head;
-  const uint16_t* t = table ? table + s * (int64_t)half * 4 : nullptr;
+  if (!live) return;
+  const uint16_t* tr = table ? table + s * (int64_t)half * 4 : nullptr;
+  uint32_t o[4];
+#pragma unroll
+  for (int i = 0; i < 8; i += 2) {
+    float r2[2];
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      const int d = 8 * t + i + k;
+      float out = rb[d];
+      if (tr && d < 2 * half) {
+        const int p = d < half ? d : d - half;
+        const uint2 e = *reinterpret_cast<const uint2*>(tr + 4 * p);  // (c, -s, s, c)
+        if (d < half) {
+          const float c = __uint_as_float(e.x << 16), ns = __uint_as_float(e.x & 0xffff0000u);
+          out = rbf(rbf(c * rb[d]) + rbf(ns * rb[d + half]));
+        } else {
+          const float sn = __uint_as_float(e.y << 16), c2 = __uint_as_float(e.y & 0xffff0000u);
+          out = rbf(rbf(sn * rb[p]) + rbf(c2 * rb[d]));
+        }
+      }
+      r2[k] = out;
+    }
+    o[i >> 1] = (uint32_t)f2bf(r2[0]) | ((uint32_t)f2bf(r2[1]) << 16);
+  }
+  *reinterpret_cast<uint4*>(y + s * y_tok + h * y_head + 8 * t) = make_uint4(o[0], o[1], o[2], o[3]);
+}
+
+// Specialisation for half == 64 (rot == head_dim, the benchmark's RoPE) and
+// for RMSNorm alone: thread t of 16 owns the rotation pairs 4t..4t+3, i.e.
+// channels 4t..4t+3 and 64+4t..64+4t+3, so each pair and its table entries
+// stay in registers.  Same arithmetic as prologue_kernel; hardware RNE
+// conversions.
+__device__ __forceinline__ float rb16(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+
+__device__ __forceinline__ void unpack4(uint2 u, float* f) {
+  f[0] = __uint_as_float(u.x << 16);
+  f[1] = __uint_as_float(u.x & 0xffff0000u);
+  f[2] = __uint_as_float(u.y << 16);
+  f[3] = __uint_as_float(u.y & 0xffff0000u);
+}
+
+__device__ __forceinline__ uint2 pack4(const float* f) {
+  __nv_bfloat162 a = __floats2bfloat162_rn(f[0], f[1]), b = __floats2bfloat162_rn(f[2], f[3]);
+  return make_uint2(*reinterpret_cast<uint32_t*>(&a), *reinterpret_cast<uint32_t*>(&b));
+}
+
+__global__ void __launch_bounds__(256) prologue_pairs_kernel(const uint16_t* __restrict__ x, int64_t x_tok,
+                                                             int64_t x_head, uint16_t* __restrict__ y, int64_t y_tok,
+                                                             int64_t y_head, int32_t seq_len, int32_t head_count,
+                                                             const uint16_t* __restrict__ w, float eps,
+                                                             const uint16_t* __restrict__ table) {
+  const int sub = threadIdx.x >> 4, t = threadIdx.x & 15;
+  const int64_t row = (int64_t)blockIdx.x * 16 + sub;
+  const bool live = row < (int64_t)seq_len * head_count;
+  const int64_t s = live ? row / head_count : 0, h = live ? row % head_count : 0;
+  float a[4], b[4], wa[4], wb[4];
+  float ss = 0.f;
+  const uint16_t* xr = x + s * x_tok + h * x_head;
+  if (live) {
+    unpack4(*reinterpret_cast<const uint2*>(xr + 4 * t), a);
+    unpack4(*reinterpret_cast<const uint2*>(xr + 64 + 4 * t), b);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) ss += a[i] * a[i] + b[i] * b[i];
+  }
+#pragma unroll
+  for (int o = 8; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffff, ss, o);
+  if (!live) return;
+  const float inv = 1.0f / sqrtf(ss / 128.f + eps);
+  unpack4(*reinterpret_cast<const uint2*>(w + 4 * t), wa);
+  unpack4(*reinterpret_cast<const uint2*>(w + 64 + 4 * t), wb);
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
-    int d = lane + 32 * i;
-    float out = rb[d];
-    if (t && d < 2 * half) {
-      if (d < half) {
-        float c = bf2f(t[4 * d]), ns = bf2f(t[4 * d + 1]);
-        out = rbf(rbf(c * rb[d]) + rbf(ns * rb[d + half]));
-      } else {
-        int p = d - half;
-        float sn = bf2f(t[4 * p + 2]), c2 = bf2f(t[4 * p + 3]);
-        out = rbf(rbf(sn * rb[p]) + rbf(c2 * rb[d]));
-      }
-    }
-    yr[d] = f2bf(out);
+    a[i] = rb16((a[i] * inv) * wa[i]);
+    b[i] = rb16((b[i] * inv) * wb[i]);
   }
+  if (table) {
+    const uint4* tp = reinterpret_cast<const uint4*>(table + (s * 64 + 4 * t) * 4);
+    const uint4 e01 = tp[0], e23 = tp[1];
+    const uint32_t ent[8] = {e01.x, e01.y, e01.z, e01.w, e23.x, e23.y, e23.z, e23.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float c = __uint_as_float(ent[2 * i] << 16), ns = __uint_as_float(ent[2 * i] & 0xffff0000u);
+      const float sn = __uint_as_float(ent[2 * i + 1] << 16), c2 = __uint_as_float(ent[2 * i + 1] & 0xffff0000u);
+      const float ra = rb16(rb16(c * a[i]) + rb16(ns * b[i]));
+      const float rb = rb16(rb16(sn * a[i]) + rb16(c2 * b[i]));
+      a[i] = ra;
+      b[i] = rb;
+    }
+  }
+  uint16_t* yr = y + s * y_tok + h * y_head;
+  *reinterpret_cast<uint2*>(yr + 4 * t) = pack4(a);
+  *reinterpret_cast<uint2*>(yr + 64 + 4 * t) = pack4(b);
 }
 
 // -------------------------------------------------------------- rope table
@@ -217,7 +302,12 @@ cudaError_t launch_prologue(const uint16_t* x, int64_t x_tok, int64_t x_head, ui
                             const uint16_t* table, int32_t half, cudaStream_t s) {
   int64_t rows = (int64_t)seq_len * head_count;
   if (rows == 0) return cudaSuccess;
-  prologue_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, s>>>(x, x_tok, x_head, y, y_tok, y_head, seq_len,
+  if (table == nullptr || half == 64) {
+    prologue_pairs_kernel<<<(unsigned)((rows + 15) / 16), 256, 0, s>>>(x, x_tok, x_head, y, y_tok, y_head, seq_len,
+                                                                        head_count, w, eps, table);
+    return cudaGetLastError();
+  }
+  prologue_kernel<<<(unsigned)((rows + 15) / 16), 256, 0, s>>>(x, x_tok, x_head, y, y_tok, y_head, seq_len,
                                                              head_count, w, eps, table, half);
   return cudaGetLastError();
 }
