@@ -158,6 +158,17 @@ h3c_status h3c_attn_fwd(h3c_ctx* ctx, const h3c_attn_args* args, void* stream);
 h3c_status h3c_attn_workspace_size(const h3c_attn_args* args, size_t* bytes);
 /* Synchronous helper for tests: h3c_attn_fwd then a stream synchronise. */
 h3c_status h3c_attn_fwd_sync(h3c_ctx* ctx, const h3c_attn_args* args, void* stream);
+/* Allocation-free variant of the fused path (H3C_FUSE_PROLOGUE required), for
+ * callers that may not call cudaMalloc (their process hands device memory to
+ * its own pool, or an allocation at call time is unacceptable).  No context:
+ * runs on the current device.  Its scratch (normalised Q and K) is a fixed
+ * 32 MiB device array inside the library, held by every GPU that loads it;
+ * ceil(S/128)*128 * head_count must be <= 65536, else H3C_ERR_CAPACITY.  The
+ * first call on a device resolves the array's address (make it before any
+ * stream capture).  All calls share the array: calls that overlap on the GPU
+ * race.  err (optional, err_len bytes) receives the message of a failure.
+ * No counterpart in the reference: its MLX path has no allocation-free mode. */
+h3c_status h3c_attn_fwd_noalloc(const h3c_attn_args* args, void* stream, char* err, size_t err_len);
 
 /* --- synthetic inputs ------------------------------------------------------ */
 /* Counter-based N(mean, std) bf16 generator; element i is a function of
