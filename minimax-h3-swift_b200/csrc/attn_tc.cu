@@ -6,9 +6,13 @@
 // order (Sources/H3Attention/AxialReference.swift:116-171 restated per block;
 // key columns past seq_len are masked).  Output bf16, O / max(l, 1e-30).
 //
-// CTA = one query block x two heads (the block list is shared by all heads,
-// so both tiles walk the same key blocks).  Roles:
-//   warp 0      TMA producer: Q tiles once, then K/V tiles into a 4-slot ring
+// CTA = two adjacent query blocks (2i, 2i+1) of one head.  Their block lists
+// overlap almost entirely (the local window of neighbouring blocks), so the
+// CTA walks the union of the two lists and every K/V tile it loads serves
+// both query tiles: half the L2->SM traffic of one query block per CTA.
+// Roles:
+//   warp 0      TMA producer: Q tiles once, then K/V of each union entry into
+//               a 4-slot ring
 //   warp 1      MMA issuer (one elected thread): S = Q K^T (SS), O += P V (TS)
 //   warp 2      TMEM allocator (512 columns)
 //   warps 4-7   softmax + epilogue of tile 0 (thread = query row = TMEM lane)
@@ -24,6 +28,7 @@
 // where TMEM is freed.
 #include <cuda.h>
 
+#include <climits>
 #include <cstdlib>
 
 #include "common.cuh"
@@ -241,11 +246,17 @@ __global__ void __launch_bounds__(kThreads, 1)
   Barriers* bars = (Barriers*)(smem + kSmemTiles);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int qb = blockIdx.x;
-  const int h0 = blockIdx.y * 2;
-  const int ntile = (h0 + 1 < a.head_count) ? 2 : 1;
-  const int p0 = a.row_ptr[qb];
-  const int nkv = a.row_ptr[qb + 1] - p0;
+  // tile t = query block 2*blockIdx.x + t of head blockIdx.y
+  const int qb0 = blockIdx.x * 2;
+  const int h = blockIdx.y;
+  const int ntile = (qb0 + 1 < a.n_blocks) ? 2 : 1;
+  int tp0[2], tn[2];
+#pragma unroll
+  for (int t = 0; t < 2; ++t) {
+    tp0[t] = t < ntile ? a.row_ptr[qb0 + t] : 0;
+    tn[t] = t < ntile ? a.row_ptr[qb0 + t + 1] - tp0[t] : 0;
+  }
+  const int nkv = tn[0] + tn[1];
   volatile int32_t* abort_flag = &bars->abort;
 
   if (threadIdx.x == 0) {
@@ -280,18 +291,19 @@ __global__ void __launch_bounds__(kThreads, 1)
    if (nkv > 0) {
     if (warp == 0) {
       // ------------------------------------------------------- TMA producer
+      // Walks the union of the two tiles' ascending block lists; every key
+      // block in the union is loaded once (K then V) and serves both tiles.
       if (lane == 0) {
         for (int t = 0; t < ntile; ++t) {
           uint32_t bar = smem_u32(&bars->q_full[t]);
           mbar_expect_tx(bar, kTileBytes);
           uint32_t dst = smem_u32(sQ + t * kTileBytes);
-          tma_load_3d(dst, &tm_q, bar, 0, qb * 128, h0 + t);
-          tma_load_3d(dst + kHalfBytes, &tm_q, bar, 64, qb * 128, h0 + t);
+          tma_load_3d(dst, &tm_q, bar, 0, (qb0 + t) * 128, h);
+          tma_load_3d(dst + kHalfBytes, &tm_q, bar, 64, (qb0 + t) * 128, h);
         }
         int n = 0;
         bool ok = true;
-        // consumption order: K_t(0) for each tile, then per j and tile: V_t(j), K_t(j+1)
-        auto load = [&](const CUtensorMap* map, int jb, int head) {
+        auto load = [&](const CUtensorMap* map, int jb) {
           const int slot = n % kStages;
           const uint32_t ph = (uint32_t)((n / kStages) & 1);
           if (!mbar_wait(smem_u32(&bars->kv_empty[slot]), ph ^ 1u, abort_flag, a.status)) {
@@ -301,16 +313,19 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint32_t bar = smem_u32(&bars->kv_full[slot]);
           mbar_expect_tx(bar, kTileBytes);
           uint32_t dst = smem_u32(sKV + slot * kTileBytes);
-          tma_load_3d(dst, map, bar, 0, jb * 128, head);
-          tma_load_3d(dst + kHalfBytes, map, bar, 64, jb * 128, head);
+          tma_load_3d(dst, map, bar, 0, jb * 128, h);
+          tma_load_3d(dst + kHalfBytes, map, bar, 64, jb * 128, h);
           ++n;
         };
-        for (int t = 0; t < ntile && ok; ++t) load(&tm_k, a.col_idx[p0], h0 + t);
-        for (int j = 0; j < nkv && ok; ++j) {
-          for (int t = 0; t < ntile && ok; ++t) {
-            load(&tm_v, a.col_idx[p0 + j], h0 + t);
-            if (ok && j + 1 < nkv) load(&tm_k, a.col_idx[p0 + j + 1], h0 + t);
-          }
+        int i0 = 0, i1 = 0;
+        while (ok && (i0 < tn[0] || i1 < tn[1])) {
+          const int c0 = i0 < tn[0] ? a.col_idx[tp0[0] + i0] : INT_MAX;
+          const int c1 = i1 < tn[1] ? a.col_idx[tp0[1] + i1] : INT_MAX;
+          const int u = min(c0, c1);
+          load(&tm_k, u);
+          if (ok) load(&tm_v, u);
+          i0 += (c0 == u);
+          i1 += (c1 == u);
         }
         // Drain: wait for the last loads to land before anyone may exit.
         if (!ok) {
@@ -324,66 +339,78 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     } else if (warp == 1) {
       // ------------------------------------------------------------ MMA issuer
+      // Union entry e owns ring items 2e (K) and 2e+1 (V).  Per entry, for
+      // each tile in turn: the PV of the tile's previous entry (its P is ready
+      // once the softmax arrives), then the tile's S for this entry, so the
+      // tiles ping-pong between MMA and softmax.  K(e) is released once the
+      // S of every tile active at e is issued; V(e) once both tiles' PVs of e
+      // are issued (at the latest while entry e+1 is processed).
       if (lane == 0) {
         constexpr uint32_t kIdS = idesc_bf16(false);
         constexpr uint32_t kIdPV = idesc_bf16(true);
         bool ok = true;
         for (int t = 0; t < ntile && ok; ++t) ok = mbar_wait(smem_u32(&bars->q_full[t]), 0, abort_flag, a.status);
         tc_fence_after();
-        int n = 0;
-        auto wait_slot = [&](int& slot) -> bool {
-          slot = n % kStages;
-          const uint32_t ph = (uint32_t)((n / kStages) & 1);
-          if (!mbar_wait(smem_u32(&bars->kv_full[slot]), ph, abort_flag, a.status)) return false;
+        int pend[2] = {-1, -1};  // union entry whose PV is still due, per tile
+        int ns[2] = {0, 0};      // S issued per tile
+        auto ring_wait = [&](int item) -> bool {
+          const int slot = item % kStages;
+          if (!mbar_wait(smem_u32(&bars->kv_full[slot]), (uint32_t)((item / kStages) & 1), abort_flag, a.status))
+            return false;
           tc_fence_after();
           return true;
         };
-        auto issue_s = [&](int t) -> bool {  // S_t = Q_t K^T
-          int slot;
-          if (!wait_slot(slot)) return false;
-          const uint32_t qa = smem_u32(sQ + t * kTileBytes);
-          const uint32_t kbase = smem_u32(sKV + slot * kTileBytes);
+        auto issue_pv = [&](int t) -> bool {
+          const int e = pend[t];
+          if (!mbar_wait(smem_u32(&bars->p_full[t]), (uint32_t)((ns[t] - 1) & 1), abort_flag, a.status)) return false;
+          tc_fence_after();
+          const int item = 2 * e + 1;
+          if (!ring_wait(item)) return false;
+          const uint32_t vbase = smem_u32(sKV + (item % kStages) * kTileBytes);
 #pragma unroll
-          for (int kk = 0; kk < 8; ++kk) {
-            const uint32_t off = (kk >> 2) * kHalfBytes + (kk & 3) * 32;
-            mma_ss(tmem + 256 * t, smem_desc(qa + off, 16, 1024), smem_desc(kbase + off, 16, 1024), kIdS,
-                   kk > 0 ? 1u : 0u);
-          }
-          tc_commit(smem_u32(&bars->kv_empty[slot]));
-          ++n;
-          return true;
-        };
-        auto issue_pv = [&](int t, int j) -> bool {  // O_t += P_t V
-          int slot;
-          if (!wait_slot(slot)) return false;
-          const uint32_t vbase = smem_u32(sKV + slot * kTileBytes);
-#pragma unroll
-          for (int kk = 0; kk < 8; ++kk) {
+          for (int kk = 0; kk < 8; ++kk)
             mma_ts(tmem + 256 * t + 128, tmem + 256 * t + kk * 8, smem_desc(vbase + kk * 2048, kHalfBytes, 1024),
-                   kIdPV, (j > 0 || kk > 0) ? 1u : 0u);
-          }
-          tc_commit(smem_u32(&bars->kv_empty[slot]));
-          ++n;
+                   kIdPV, (ns[t] > 1 || kk > 0) ? 1u : 0u);
+          pend[t] = -1;
+          if (pend[t ^ 1] != e) tc_commit(smem_u32(&bars->kv_empty[item % kStages]));
           return true;
         };
-        for (int t = 0; t < ntile && ok; ++t) {
-          ok = issue_s(t);
-          if (ok) tc_commit(smem_u32(&bars->s_full[t]));
-        }
-        for (int j = 0; j < nkv && ok; ++j) {
-          for (int t = 0; t < ntile && ok; ++t) {
-            ok = mbar_wait(smem_u32(&bars->p_full[t]), (uint32_t)(j & 1), abort_flag, a.status);
-            if (!ok) break;
-            tc_fence_after();
-            ok = issue_pv(t, j);
-            if (!ok) break;
-            if (j + 1 < nkv) {
-              ok = issue_s(t);
-              if (ok) tc_commit(smem_u32(&bars->s_full[t]));
-            } else {
-              tc_commit(smem_u32(&bars->o_full[t]));
+        int i0 = 0, i1 = 0, e = 0;
+        while (ok && (i0 < tn[0] || i1 < tn[1])) {
+          const int c0 = i0 < tn[0] ? a.col_idx[tp0[0] + i0] : INT_MAX;
+          const int c1 = i1 < tn[1] ? a.col_idx[tp0[1] + i1] : INT_MAX;
+          const int u = min(c0, c1);
+          const bool act[2] = {c0 == u, c1 == u};
+          bool kwaited = false;
+          for (int t = 0; t < 2 && ok; ++t) {
+            if (pend[t] >= 0) ok = issue_pv(t);
+            if (ok && act[t]) {
+              if (!kwaited) {
+                ok = ring_wait(2 * e);
+                kwaited = true;
+                if (!ok) break;
+              }
+              const uint32_t qa = smem_u32(sQ + t * kTileBytes);
+              const uint32_t kbase = smem_u32(sKV + ((2 * e) % kStages) * kTileBytes);
+#pragma unroll
+              for (int kk = 0; kk < 8; ++kk) {
+                const uint32_t off = (kk >> 2) * kHalfBytes + (kk & 3) * 32;
+                mma_ss(tmem + 256 * t, smem_desc(qa + off, 16, 1024), smem_desc(kbase + off, 16, 1024), kIdS,
+                       kk > 0 ? 1u : 0u);
+              }
+              tc_commit(smem_u32(&bars->s_full[t]));
+              pend[t] = e;
+              ++ns[t];
             }
           }
+          if (ok) tc_commit(smem_u32(&bars->kv_empty[(2 * e) % kStages]));
+          i0 += act[0];
+          i1 += act[1];
+          ++e;
+        }
+        for (int t = 0; t < ntile && ok; ++t) {
+          if (pend[t] >= 0) ok = issue_pv(t);
+          if (ok) tc_commit(smem_u32(&bars->o_full[t]));
         }
         if (!ok) {  // let every issued MMA retire before TMEM is released
           tc_commit(smem_u32(&bars->o_full[0]));
@@ -398,7 +425,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       // --------------------------------------------------- softmax + epilogue
       const int t = (warp - 4) >> 2;
       const int q = warp & 3;  // TMEM lane quarter this warp may access
-      if (t < ntile) {
+      if (t < ntile && tn[t] > 0) {
+        const int p0 = tp0[t];
+        const int nkv = tn[t];
         const uint32_t lane_base = (uint32_t)(32 * q) << 16;
         const uint32_t tS = tmem + lane_base + 256 * t;
         const uint32_t tO = tS + 128;
@@ -485,9 +514,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (ok && mbar_wait(smem_u32(&bars->o_full[t]), 0, abort_flag, a.status)) {
           tc_fence_after();
-          const int row = qb * 128 + 32 * q + lane;
+          const int row = (qb0 + t) * 128 + 32 * q + lane;
           const float inv = 1.0f / fmaxf(l, 1e-30f);
-          uint16_t* go = a.o + (int64_t)(h0 + t) * a.o_head + (int64_t)row * a.o_tok;
+          uint16_t* go = a.o + (int64_t)h * a.o_head + (int64_t)row * a.o_tok;
 #pragma unroll
           for (int c = 0; c < 8; ++c) {
             uint32_t o[16];
@@ -611,7 +640,7 @@ cudaError_t launch_attn_tc(const AttnLaunch& a, cudaStream_t s, std::string* err
     emu = env ? atoi(env) : kDefaultEmu;
     if (emu < 0 || emu > 8) emu = kDefaultEmu;
   }
-  dim3 grid(a.n_blocks, (a.head_count + 1) / 2);
+  dim3 grid((a.n_blocks + 1) / 2, a.head_count);
   switch (emu) {
     case 0: return launch_variant<0>(grid, s, mq, mk, mv, a);
     case 2: return launch_variant<2>(grid, s, mq, mk, mv, a);
