@@ -140,8 +140,8 @@ class CpuBaseline:
         step = max(self.threads, 8)
         done_flops, elapsed, used = 0.0, 0.0, 0
         while elapsed < budget_s and used < nb:
-            idx = [(self.cursor + i) % nb for i in range(step)]
-            self.cursor = (self.cursor + step) % nb
+            idx = [(self.cursor + i) % nb for i in range(min(step, nb - used))]
+            self.cursor = (self.cursor + len(idx)) % nb
             qbs = self.order[idx]
             used += len(qbs)
             t0 = time.perf_counter()
@@ -189,8 +189,9 @@ def run_reference(args):
 
 # Per-launch DRAM traffic of attn_tc_kernel on config2 (dram__bytes_read.sum +
 # dram__bytes_write.sum), from the ncu capture summarised in
-# profiles/attn_tc_kernel_config2.md; None until that capture exists.
-TRAFFIC_BYTES = {}
+# profiles/attn_tc_kernel_config2.md (captured at 8 heads, scaled by 40/8);
+# None for workloads without a capture.
+TRAFFIC_BYTES = {"config2": 6.06e9}
 
 
 def _timed(fn, steps):
