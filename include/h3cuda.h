@@ -156,7 +156,14 @@ h3c_status h3c_prologue(h3c_ctx* ctx, h3c_view x, h3c_view out, int32_t seq_len,
 h3c_status h3c_attn_fwd(h3c_ctx* ctx, const h3c_attn_args* args, void* stream);
 /* Bytes of workspace h3c_attn_fwd needs for these args. */
 h3c_status h3c_attn_workspace_size(const h3c_attn_args* args, size_t* bytes);
-/* Synchronous helper for tests: h3c_attn_fwd then a stream synchronise. */
+/* Reads (and clears) the status word the attention kernel writes when one of
+ * its bounded device waits gives up: H3C_OK, or H3C_ERR_TIMEOUT (the output
+ * of that call is invalid; the context stays usable).  Synchronous.  The
+ * bounded waits replace the reference's render-level cancellation
+ * (Sources/MiniMaxH3/RenderEngine.swift:574-590) at the kernel level. */
+h3c_status h3c_device_status(h3c_ctx* ctx);
+/* Synchronous helper for tests: h3c_attn_fwd, a stream synchronise, then
+ * h3c_device_status. */
 h3c_status h3c_attn_fwd_sync(h3c_ctx* ctx, const h3c_attn_args* args, void* stream);
 /* Allocation-free variant of the fused path (H3C_FUSE_PROLOGUE required), for
  * callers that may not call cudaMalloc (their process hands device memory to

@@ -2,6 +2,7 @@
 // block-mask builder and dispatch to the kernels.  Every entry point returns
 // a status; nothing here aborts or exits.
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <new>
 #include <vector>
@@ -147,7 +148,7 @@ h3c_status h3c_init(int device, h3c_ctx** out) {
     delete ctx;
     return H3C_ERR_NO_DEVICE;
   }
-  if (cudaMalloc(&ctx->d_counter, 64) != cudaSuccess) {
+  if (cudaMalloc(&ctx->d_counter, 64) != cudaSuccess || cudaMemset(ctx->d_counter, 0, 64) != cudaSuccess) {
     delete ctx;
     return H3C_ERR_CUDA;
   }
@@ -353,6 +354,13 @@ h3c_status h3c_attn_fwd(h3c_ctx* ctx, const h3c_attn_args* args, void* stream) {
     L.q = qn; L.q_tok = (int64_t)a.head_count * 128; L.q_head = 128;
   }
 
+  L.status = (int32_t*)(ctx->d_counter + 1);
+  L.wait_limit_ns = 4000000000ull;
+  L.drop_item = -1;
+  // Test hooks (fault injection on the host side): a K/V load the producer
+  // skips, so that the consumers' bounded waits run out, and a shorter bound.
+  if (const char* d = getenv("H3C_TEST_DROP_ITEM")) L.drop_item = atoi(d);
+  if (const char* w = getenv("H3C_TEST_WAIT_LIMIT_NS")) L.wait_limit_ns = strtoull(w, nullptr, 10);
   cudaError_t e;
   if (a.flags & H3C_KERNEL_MMA_SYNC) {
     e = h3::launch_attn_mma(L, s);
@@ -369,7 +377,17 @@ h3c_status h3c_attn_fwd_sync(h3c_ctx* ctx, const h3c_attn_args* args, void* stre
   h3c_status st = h3c_attn_fwd(ctx, args, stream);
   if (st != H3C_OK) return st;
   H3_CUDA_TRY(ctx, cudaStreamSynchronize((cudaStream_t)stream));
-  return H3C_OK;
+  return h3c_device_status(ctx);
+}
+
+h3c_status h3c_device_status(h3c_ctx* ctx) {
+  if (!ctx) return H3C_ERR_INVALID_ARGUMENT;
+  H3_CUDA_TRY(ctx, cudaSetDevice(ctx->device));
+  int32_t word = 0;
+  H3_CUDA_TRY(ctx, cudaMemcpy(&word, ctx->d_counter + 1, sizeof(word), cudaMemcpyDeviceToHost));
+  if (word == 0) return H3C_OK;
+  H3_CUDA_TRY(ctx, cudaMemset(ctx->d_counter + 1, 0, sizeof(int64_t)));
+  return fail(ctx, (h3c_status)word, "h3c_attn_fwd: a bounded device wait gave up (H3C_ERR_TIMEOUT); output invalid");
 }
 
 h3c_status h3c_fill_normal_bf16(h3c_ctx* ctx, void* d_out, int64_t n, uint64_t seed, uint64_t stream_id, double mean,

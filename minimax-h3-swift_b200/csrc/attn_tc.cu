@@ -83,14 +83,14 @@ __device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
 
 // Bounded wait; false on abort/timeout.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int32_t* abort_flag,
-                                          int32_t* status) {
+                                          int32_t* status, uint64_t limit_ns = kWaitLimitNs) {
   for (int i = 0; i < 64; ++i)
     if (mbar_try(bar, parity)) return true;
   const uint64_t t0 = globaltimer();
   while (true) {
     if (mbar_try(bar, parity)) return true;
     if (*abort_flag) return false;
-    if (globaltimer() - t0 > kWaitLimitNs) {
+    if (globaltimer() - t0 > limit_ns) {
       *abort_flag = 1;
       if (status) atomicExch(status, (int32_t)H3C_ERR_TIMEOUT);
       return false;
@@ -306,7 +306,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         auto load = [&](const CUtensorMap* map, int jb) {
           const int slot = n % kStages;
           const uint32_t ph = (uint32_t)((n / kStages) & 1);
-          if (!mbar_wait(smem_u32(&bars->kv_empty[slot]), ph ^ 1u, abort_flag, a.status)) {
+          if (n == a.drop_item) {  // host-side fault injection for tests: this load never happens
+            ++n;
+            return;
+          }
+          if (!mbar_wait(smem_u32(&bars->kv_empty[slot]), ph ^ 1u, abort_flag, a.status, a.wait_limit_ns)) {
             ok = false;
             return;
           }
@@ -349,20 +353,20 @@ __global__ void __launch_bounds__(kThreads, 1)
         constexpr uint32_t kIdS = idesc_bf16(false);
         constexpr uint32_t kIdPV = idesc_bf16(true);
         bool ok = true;
-        for (int t = 0; t < ntile && ok; ++t) ok = mbar_wait(smem_u32(&bars->q_full[t]), 0, abort_flag, a.status);
+        for (int t = 0; t < ntile && ok; ++t) ok = mbar_wait(smem_u32(&bars->q_full[t]), 0, abort_flag, a.status, a.wait_limit_ns);
         tc_fence_after();
         int pend[2] = {-1, -1};  // union entry whose PV is still due, per tile
         int ns[2] = {0, 0};      // S issued per tile
         auto ring_wait = [&](int item) -> bool {
           const int slot = item % kStages;
-          if (!mbar_wait(smem_u32(&bars->kv_full[slot]), (uint32_t)((item / kStages) & 1), abort_flag, a.status))
+          if (!mbar_wait(smem_u32(&bars->kv_full[slot]), (uint32_t)((item / kStages) & 1), abort_flag, a.status, a.wait_limit_ns))
             return false;
           tc_fence_after();
           return true;
         };
         auto issue_pv = [&](int t) -> bool {
           const int e = pend[t];
-          if (!mbar_wait(smem_u32(&bars->p_full[t]), (uint32_t)((ns[t] - 1) & 1), abort_flag, a.status)) return false;
+          if (!mbar_wait(smem_u32(&bars->p_full[t]), (uint32_t)((ns[t] - 1) & 1), abort_flag, a.status, a.wait_limit_ns)) return false;
           tc_fence_after();
           const int item = 2 * e + 1;
           if (!ring_wait(item)) return false;
@@ -439,7 +443,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int last_valid = a.seq_len - a.col_idx[p0 + nkv - 1] * 128;
         const uint64_t sl2x2 = dup2(sl2);
         for (int j = 0; j < nkv; ++j) {
-          if (!mbar_wait(smem_u32(&bars->s_full[t]), (uint32_t)(j & 1), abort_flag, a.status)) {
+          if (!mbar_wait(smem_u32(&bars->s_full[t]), (uint32_t)(j & 1), abort_flag, a.status, a.wait_limit_ns)) {
             ok = false;
             break;
           }
@@ -512,7 +516,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           tc_fence_before();
           mbar_arrive(smem_u32(&bars->p_full[t]));
         }
-        if (ok && mbar_wait(smem_u32(&bars->o_full[t]), 0, abort_flag, a.status)) {
+        if (ok && mbar_wait(smem_u32(&bars->o_full[t]), 0, abort_flag, a.status, a.wait_limit_ns)) {
           tc_fence_after();
           const int row = (qb0 + t) * 128 + 32 * q + lane;
           const float inv = 1.0f / fmaxf(l, 1e-30f);

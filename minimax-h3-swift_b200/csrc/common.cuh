@@ -15,7 +15,7 @@ struct h3c_ctx {
   cudaDeviceProp prop{};
   void* workspace = nullptr;      // normalised keys/queries of the fused path
   size_t workspace_bytes = 0;
-  int64_t* d_counter = nullptr;   // small device scratch (mask builder nnz)
+  int64_t* d_counter = nullptr;   // small device scratch: [0] mask builder nnz, [1] kernel status word
 };
 
 namespace h3 {
@@ -75,6 +75,8 @@ struct AttnLaunch {
   // fused Q prologue (tcgen05 path only); q_norm == nullptr means q is final
   const uint16_t* q_norm; const uint16_t* rope; int32_t rope_half; float eps;
   int32_t* status;                // device status word (bounded waits), may be null
+  uint64_t wait_limit_ns;         // bound of every mbarrier wait
+  int32_t drop_item;              // test hook: K/V ring item the producer skips (-1: none)
 };
 
 cudaError_t launch_attn_mma(const AttnLaunch& a, cudaStream_t s);

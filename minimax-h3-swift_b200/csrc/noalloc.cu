@@ -138,6 +138,9 @@ extern "C" h3c_status h3c_attn_fwd_noalloc(const h3c_attn_args* args, void* stre
   L.scale_log2 = a.scale * 1.4426950408889634f;
   L.row_ptr = a.row_ptr;
   L.col_idx = a.col_idx;
+  L.status = nullptr;
+  L.wait_limit_ns = 4000000000ull;
+  L.drop_item = -1;
   std::string why;
   e = h3::launch_attn_tc(L, s, &why);
   if (e != cudaSuccess) {

@@ -36,7 +36,7 @@ EXPORTS = (
     "h3c_abi_version", "h3c_init", "h3c_destroy", "h3c_last_error", "h3c_device_info",
     "h3c_device_count", "h3c_blockmask_build", "h3c_blockmask_build_device", "h3c_rope_table",
     "h3c_prologue", "h3c_attn_fwd", "h3c_attn_workspace_size", "h3c_attn_fwd_sync",
-    "h3c_fill_normal_bf16", "h3c_attn_fwd_noalloc",
+    "h3c_fill_normal_bf16", "h3c_attn_fwd_noalloc", "h3c_device_status",
 )
 
 
@@ -112,6 +112,7 @@ def load() -> C.CDLL:
             "h3c_attn_workspace_size": ([C.POINTER(AttnArgs), C.POINTER(C.c_size_t)], st),
             "h3c_attn_fwd_sync": ([vp, C.POINTER(AttnArgs), vp], st),
             "h3c_fill_normal_bf16": ([vp, vp, i64, u64, u64, f64, f64, vp], st),
+            "h3c_device_status": ([vp], st),
             "h3c_attn_fwd_noalloc": ([C.POINTER(AttnArgs), vp, C.c_char_p, C.c_size_t], st),
         }
         for name, (args, res) in sig.items():

@@ -104,6 +104,15 @@ class Runtime:
         a = self.attn_args(**kw)
         self._check(self.L.h3c_attn_fwd(self.ctx, C.byref(a), _stream_ptr(stream)))
 
+    def attn_fwd_sync(self, *, stream=None, **kw):
+        """attn_fwd, synchronise, and raise H3CError(H3C_ERR_TIMEOUT) if a
+        bounded device wait gave up."""
+        a = self.attn_args(**kw)
+        self._check(self.L.h3c_attn_fwd_sync(self.ctx, C.byref(a), _stream_ptr(stream)))
+
+    def device_status(self):
+        self._check(self.L.h3c_device_status(self.ctx))
+
     def attn_fwd_args(self, a: _lib.AttnArgs, stream=None):
         self._check(self.L.h3c_attn_fwd(self.ctx, C.byref(a), _stream_ptr(stream)))
 
