@@ -211,6 +211,7 @@ def run_ours(args):
     import torch.distributed as dist
 
     from h3attention import BlockList, Runtime
+    from h3attention.sharding import cuda_attend_fn, head_range, seq_shard_len, ulysses_attend
     from h3attention.configs import EPS, ROPE_DIMS, ROPE_THETA, STREAM_K, STREAM_Q, STREAM_V, STREAM_WK, STREAM_WQ
 
     ws, rank, local = _dist()
@@ -226,18 +227,42 @@ def run_ours(args):
     def fill(shape, stream, mean=0.0, std=1.0):
         return rt.fill_normal(torch.empty(shape, dtype=bf, device=dev), wl.seed + rank, stream, mean, std)
 
-    q, k, v = fill((S, H, 128), STREAM_Q), fill((S, H, 128), STREAM_K), fill((S, H, 128), STREAM_V)
+    mode = args.mode if ws > 1 else "replica"
+    # rows (tokens) and heads this rank holds
+    if mode == "heads":
+        h0, h1 = head_range(rank, ws, H)
+        rows, hl = S, h1 - h0
+    elif mode == "seq":
+        rows, hl = seq_shard_len(S, ws), H
+    else:
+        rows, hl = S, H
+    q, k, v = fill((rows, hl, 128), STREAM_Q), fill((rows, hl, 128), STREAM_K), fill((rows, hl, 128), STREAM_V)
     wq, wk = fill((128,), STREAM_WQ, 1.0, 0.02), fill((128,), STREAM_WK, 1.0, 0.02)
     tab = rt.rope_table(torch.from_numpy(wl.positions()).to(dev), ROPE_DIMS, ROPE_THETA)
     bl = BlockList.build(wl.mask_spec())
     blocks = bl.on(dev)
-    flops = bl.flops(H)
-    out = torch.empty_like(q)
     scale = 128 ** -0.5
-    fused = rt.attn_args(q, k, v, out, "SHD", scale, blocks, q_norm=wq, k_norm=wk, eps=EPS, rope_table=tab)
+    if mode == "seq":
+        # every rank: all-to-all, the fused call on H/P heads of the whole
+        # sequence, all-to-all back; the work of one call is shared
+        attend = cuda_attend_fn(rt, blocks, S, scale, q_norm=wq, k_norm=wk, eps=EPS, rope_table=tab)
+        job_flops = bl.flops(H)
+        out = torch.empty_like(q)
 
-    def step():
-        rt.attn_fwd_args(fused)
+        def step():
+            out.copy_(ulysses_attend(q, k, v, S, attend))
+
+        fused = None
+        scaling = "strong"
+    else:
+        out = torch.empty_like(q)
+        fused = rt.attn_args(q, k, v, out, "SHD", scale, blocks, q_norm=wq, k_norm=wk, eps=EPS, rope_table=tab)
+        job_flops = bl.flops(H) * (ws if mode == "replica" else 1)  # the whole job's work
+        scaling = "weak" if mode == "replica" else "strong"
+
+        def step():
+            rt.attn_fwd_args(fused)
+    flops = bl.flops(hl if mode != "seq" else H // ws)  # this rank's attention work per call
 
     for _ in range(args.warmup):
         step()
@@ -252,15 +277,22 @@ def run_ours(args):
         t = torch.tensor([ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
-    value = ws * flops / (ms * 1e-3) / 1e12
+    value = job_flops / (ms * 1e-3) / 1e12
     launches = 3 * args.steps  # K prologue, Q prologue, attention per call
 
     # Roofline pass: the attention kernel alone on pre-normalised Q/K, each
     # launch bracketed by events on the launching stream.
-    qn, kn = torch.empty_like(q), torch.empty_like(k)
-    rt.prologue(q, qn, wq, EPS, tab)
-    rt.prologue(k, kn, wk, EPS, tab)
-    plain = rt.attn_args(qn, kn, v, out, "SHD", scale, blocks)
+    if mode == "seq":  # the per-rank kernel runs on [S, H/P] after the exchange
+        rq, rk, rv = (torch.empty((S, H // ws, 128), dtype=bf, device=dev) for _ in range(3))
+        for t_, st_ in ((rq, STREAM_Q), (rk, STREAM_K), (rv, STREAM_V)):
+            rt.fill_normal(t_, wl.seed + rank, st_)
+        rout = torch.empty_like(rq)
+    else:
+        rq, rk, rv, rout = q, k, v, out
+    qn, kn = torch.empty_like(rq), torch.empty_like(rk)
+    rt.prologue(rq, qn, wq, EPS, tab[: rq.shape[0]])
+    rt.prologue(rk, kn, wk, EPS, tab[: rk.shape[0]])
+    plain = rt.attn_args(qn, kn, rv, rout, "SHD", scale, blocks)
     for _ in range(2):
         rt.attn_fwd_args(plain)
     times = []
@@ -283,7 +315,7 @@ def run_ours(args):
         q.copy_(hq, non_blocking=True)
         k.copy_(hk, non_blocking=True)
         v.copy_(hv, non_blocking=True)
-        rt.attn_fwd_args(fused)
+        step()
         hout.copy_(out, non_blocking=True)
 
     e2e_step()
@@ -302,13 +334,15 @@ def run_ours(args):
         traffic = TRAFFIC_BYTES.get(wl.name)
         line = {
             "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": ws, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": scaling,
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1) bf16; shapes of the workload)",
             "config": {"workload": wl.name, "seq_len": S, "heads": H, "head_dim": 128, "block": 128,
                        "density": round(bl.density, 4), "kept_blocks": bl.nnz, "flops_per_call": flops,
-                       "l2": "inputs larger than L2 (no flush)", "parallelism": f"replicas x{ws} (weak)",
+                       "l2": "inputs larger than L2 (no flush)",
+                       "parallelism": {"replica": f"replicas x{ws} (weak)", "heads": f"head-sharded x{ws}",
+                                       "seq": f"sequence-sharded x{ws} (NCCL all-to-all)"}[mode],
                        "prologue": "fused RMSNorm + RoPE (t/h/w 32/48/48, theta 1e4)"},
-            "e2e": {"value": ws * flops / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": e2e_ms,
+            "e2e": {"value": job_flops / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": e2e_ms,
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
             "roofline": {"bound": "tensor", "kernel": "attn_tc_kernel", "achieved": achieved,
                          "peak": peaks["bf16_tflops"], "unit": "TFLOP/s", "frac": achieved / peaks["bf16_tflops"],
@@ -335,6 +369,9 @@ def main():
     ap.add_argument("--config", default="config2",
                     help="config1..config4 or config5@<density>; default config2 (the 5 s 1344x768 clip)")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--mode", default="replica", choices=["replica", "heads", "seq"],
+                    help="N>1 layout: independent full calls per rank (weak), heads split across ranks, or "
+                         "sequence-sharded with an all-to-all (strong)")
     ap.add_argument("--cpu-budget", type=float, default=15.0, help="seconds of CPU baseline sampling")
     ap.add_argument("--ref-budget", type=float, default=120.0, help="total seconds for --impl reference")
     ap.add_argument("--no-cpu-baseline", action="store_true")

@@ -1,0 +1,75 @@
+"""Sequence-sharded (Ulysses) attention on 2 GPUs over NCCL, against the
+single-GPU fused call on the same inputs.  Skipped with fewer than 2 GPUs."""
+import os
+import socket
+
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+
+def _port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, q_out):
+    import sys
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    sys.path[:0] = [root, os.path.join(root, "minimax-h3-swift_b200")]
+    import torch
+    import torch.distributed as dist
+
+    from h3attention import BlockList, Runtime
+    from h3attention.configs import CONFIGS, EPS
+    from h3attention.sharding import cuda_attend_fn, seq_shard_len, ulysses_attend
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev)
+    try:
+        wl = CONFIGS["config1"]
+        S, H = wl.seq_len, wl.heads
+        rt = Runtime.get(rank)
+        n = seq_shard_len(S, world)
+        full = [rt.fill_normal(torch.empty((n * world, H, 128), dtype=torch.bfloat16, device=dev), 5, st)
+                for st in (1, 2, 3)]
+        wq, wk = (rt.fill_normal(torch.empty(128, dtype=torch.bfloat16, device=dev), 5, st, 1.0, 0.02)
+                  for st in (4, 5))
+        tab = rt.rope_table(torch.from_numpy(wl.positions()).to(dev))
+        bl = BlockList.build(wl.mask_spec())
+        attend = cuda_attend_fn(rt, bl.on(dev), S, 128 ** -0.5, q_norm=wq, k_norm=wk, eps=EPS, rope_table=tab)
+        mine = [t[rank * n:(rank + 1) * n].contiguous() for t in full]
+        out = ulysses_attend(*mine, S, attend)
+        want = torch.empty_like(full[0])
+        rt.attn_fwd(q=full[0][:S], k=full[1][:S], v=full[2][:S], out=want[:S], layout="SHD", scale=128 ** -0.5,
+                    blocks=bl.on(dev), q_norm=wq, k_norm=wk, eps=EPS, rope_table=tab)
+        torch.cuda.synchronize()
+        lo, hi = rank * n, min(S, (rank + 1) * n)
+        d = (out[: hi - lo].float() - want[lo:hi].float()).abs()
+        q_out.put((rank, d.max().item()))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_ulysses_two_gpus_matches_single_gpu(gpu):
+    import torch
+    import torch.multiprocessing as mp
+
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=300) for _ in range(2)]
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    for rank, err in res:
+        assert err == 0.0, (rank, err)  # same kernels, same per-head inputs
