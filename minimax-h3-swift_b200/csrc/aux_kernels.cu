@@ -82,9 +82,8 @@ __global__ void __launch_bounds__(256) prologue_kernel(const uint16_t* __restric
 // Specialisation for half == 64 (rot == head_dim, the benchmark's RoPE) and
 // for RMSNorm alone: thread t of 16 owns the rotation pairs 4t..4t+3, i.e.
 // channels 4t..4t+3 and 64+4t..64+4t+3, so each pair and its table entries
-// stay in registers.  Same arithmetic as prologue_kernel; hardware RNE
-// conversions.
-__device__ __forceinline__ float rb16(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+// stay in registers.  Same arithmetic as prologue_kernel, with the rotation
+// on packed bf16x2 operations.
 
 __device__ __forceinline__ void unpack4(uint2 u, float* f) {
   f[0] = __uint_as_float(u.x << 16);
@@ -93,10 +92,6 @@ __device__ __forceinline__ void unpack4(uint2 u, float* f) {
   f[3] = __uint_as_float(u.y & 0xffff0000u);
 }
 
-__device__ __forceinline__ uint2 pack4(const float* f) {
-  __nv_bfloat162 a = __floats2bfloat162_rn(f[0], f[1]), b = __floats2bfloat162_rn(f[2], f[3]);
-  return make_uint2(*reinterpret_cast<uint32_t*>(&a), *reinterpret_cast<uint32_t*>(&b));
-}
 
 __global__ void __launch_bounds__(256) prologue_pairs_kernel(const uint16_t* __restrict__ x, int64_t x_tok,
                                                              int64_t x_head, uint16_t* __restrict__ y, int64_t y_tok,
@@ -122,28 +117,40 @@ __global__ void __launch_bounds__(256) prologue_pairs_kernel(const uint16_t* __r
   const float inv = 1.0f / sqrtf(ss / 128.f + eps);
   unpack4(*reinterpret_cast<const uint2*>(w + 4 * t), wa);
   unpack4(*reinterpret_cast<const uint2*>(w + 64 + 4 * t), wb);
+  // normalised pairs as bf16x2 words: A[k] = channels 4t+2k, 4t+2k+1;
+  // B[k] = the partners 64 channels up
+  __nv_bfloat162 A[2], B[2];
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    a[i] = rb16((a[i] * inv) * wa[i]);
-    b[i] = rb16((b[i] * inv) * wb[i]);
+  for (int k = 0; k < 2; ++k) {
+    A[k] = __floats2bfloat162_rn((a[2 * k] * inv) * wa[2 * k], (a[2 * k + 1] * inv) * wa[2 * k + 1]);
+    B[k] = __floats2bfloat162_rn((b[2 * k] * inv) * wb[2 * k], (b[2 * k + 1] * inv) * wb[2 * k + 1]);
   }
   if (table) {
+    // Each product and each sum rounded to bf16 once: bf16 x bf16 is exact
+    // in fp32, and where fp32 would round a sum of two bf16 values the bf16
+    // result is the larger operand either way, so the packed bf16 ops (no
+    // contraction) equal the fp32-then-round steps of the reference.
     const uint4* tp = reinterpret_cast<const uint4*>(table + (s * 64 + 4 * t) * 4);
-    const uint4 e01 = tp[0], e23 = tp[1];
-    const uint32_t ent[8] = {e01.x, e01.y, e01.z, e01.w, e23.x, e23.y, e23.z, e23.w};
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const float c = __uint_as_float(ent[2 * i] << 16), ns = __uint_as_float(ent[2 * i] & 0xffff0000u);
-      const float sn = __uint_as_float(ent[2 * i + 1] << 16), c2 = __uint_as_float(ent[2 * i + 1] & 0xffff0000u);
-      const float ra = rb16(rb16(c * a[i]) + rb16(ns * b[i]));
-      const float rb = rb16(rb16(sn * a[i]) + rb16(c2 * b[i]));
-      a[i] = ra;
-      b[i] = rb;
+    for (int k = 0; k < 2; ++k) {
+      const uint4 e = tp[k];  // entries 4t+2k and 4t+2k+1: (c, -s, s, c) each
+      const uint32_t cw = __byte_perm(e.x, e.z, 0x5410), nsw = __byte_perm(e.x, e.z, 0x7632);
+      const uint32_t sw = __byte_perm(e.y, e.w, 0x5410), c2w = __byte_perm(e.y, e.w, 0x7632);
+      const __nv_bfloat162 c = *reinterpret_cast<const __nv_bfloat162*>(&cw);
+      const __nv_bfloat162 ns = *reinterpret_cast<const __nv_bfloat162*>(&nsw);
+      const __nv_bfloat162 sn = *reinterpret_cast<const __nv_bfloat162*>(&sw);
+      const __nv_bfloat162 c2 = *reinterpret_cast<const __nv_bfloat162*>(&c2w);
+      const __nv_bfloat162 ra = __hadd2_rn(__hmul2_rn(c, A[k]), __hmul2_rn(ns, B[k]));
+      const __nv_bfloat162 rbv = __hadd2_rn(__hmul2_rn(sn, A[k]), __hmul2_rn(c2, B[k]));
+      A[k] = ra;
+      B[k] = rbv;
     }
   }
   uint16_t* yr = y + s * y_tok + h * y_head;
-  *reinterpret_cast<uint2*>(yr + 4 * t) = pack4(a);
-  *reinterpret_cast<uint2*>(yr + 64 + 4 * t) = pack4(b);
+  *reinterpret_cast<uint2*>(yr + 4 * t) =
+      make_uint2(*reinterpret_cast<uint32_t*>(&A[0]), *reinterpret_cast<uint32_t*>(&A[1]));
+  *reinterpret_cast<uint2*>(yr + 64 + 4 * t) =
+      make_uint2(*reinterpret_cast<uint32_t*>(&B[0]), *reinterpret_cast<uint32_t*>(&B[1]));
 }
 
 // -------------------------------------------------------------- rope table
