@@ -306,17 +306,30 @@ def run_ours(args):
     attn_ms = statistics.mean(a.elapsed_time(b) for a, b in times)
     del qn, kn
 
-    # End to end through the public call with host buffers: pinned host
-    # q/k/v -> device, the fused call, result -> pinned host, every step.
-    hq, hk, hv = (t.cpu().pin_memory() for t in (q, k, v))
-    hout = torch.empty(out.shape, dtype=bf).pin_memory()
+    # End to end through the public host-buffer call (h3attention.host):
+    # pinned host [H, S, D] q/k/v in, fused call, pinned host output back,
+    # every step; uploads, compute and downloads of head chunks overlap.
+    if mode == "seq":
+        hq, hk, hv = (t.cpu().pin_memory() for t in (q, k, v))
+        hout = torch.empty(out.shape, dtype=bf).pin_memory()
 
-    def e2e_step():
-        q.copy_(hq, non_blocking=True)
-        k.copy_(hk, non_blocking=True)
-        v.copy_(hv, non_blocking=True)
-        step()
-        hout.copy_(out, non_blocking=True)
+        def e2e_step():
+            q.copy_(hq, non_blocking=True)
+            k.copy_(hk, non_blocking=True)
+            v.copy_(hv, non_blocking=True)
+            step()
+            hout.copy_(out, non_blocking=True)
+    else:
+        from h3attention.host import HostAttention
+
+        hq, hk, hv = (t.transpose(0, 1).contiguous().cpu().pin_memory() for t in (q, k, v))
+        hout = torch.empty(hq.shape, dtype=bf).pin_memory()
+        del q, k, v, out, fused, plain, rq, rk, rv, rout
+        torch.cuda.empty_cache()
+        ha = HostAttention(local, hl, S, chunk_heads=args.chunk_heads)
+
+        def e2e_step():
+            ha(hq, hk, hv, hout, blocks, scale, q_norm=wq, k_norm=wk, eps=EPS, rope_table=tab)
 
     e2e_step()
     torch.cuda.synchronize()
@@ -325,8 +338,8 @@ def run_ours(args):
         t = torch.tensor([e2e_ms, attn_ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_ms, attn_ms = (float(x) for x in t.tolist())
-    h2d = 3 * q.numel() * 2
-    d2h = out.numel() * 2
+    h2d = 3 * hq.numel() * 2
+    d2h = hout.numel() * 2
 
     if rank == 0:
         peaks, src = _peaks()
@@ -375,6 +388,7 @@ def main():
     ap.add_argument("--cpu-budget", type=float, default=15.0, help="seconds of CPU baseline sampling")
     ap.add_argument("--ref-budget", type=float, default=120.0, help="total seconds for --impl reference")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--chunk-heads", type=int, default=2, help="heads per pipeline stage of the e2e host call")
     ap.add_argument("--heads", type=int, default=None,
                     help="override the workload's head count (small profiling cases only)")
     args = ap.parse_args()

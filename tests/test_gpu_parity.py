@@ -216,3 +216,31 @@ def test_full_size_config2_sampled(gpu):
     want = O.attend_streaming(qh, kh, vh, bl.row_ptr, bl.col_idx, qblocks=qbs)
     rows = np.concatenate([np.arange(b * 128, min(S, b * 128 + 128)) for b in qbs])
     _check_attn(_np(out[:, heads[0]:heads[1]]), want, rows=rows)
+
+
+def test_host_pipeline_matches_device_call(gpu):
+    """h3attention.host.HostAttention (pinned host [H,S,D] in/out, head
+    chunks overlapped on three streams) equals the device call."""
+    import torch
+
+    from h3attention import BlockList, MaskSpec, Runtime
+    from h3attention.host import HostAttention
+
+    S, H = 2000, 6
+    spec = MaskSpec(seq_len=S, frames=5, height=20, width=20, n_random=2, seed=4)
+    bl = BlockList.build(spec)
+    q, k, v = (O.fill_normal_bf16((H, S, 128), 17, st) for st in (1, 2, 3))
+    wq, wk = (_t(O.fill_normal_bf16((128,), 17, st, 1.0, 0.02), gpu) for st in (4, 5))
+    pos = np.stack([np.arange(S) // 400, (np.arange(S) // 20) % 20, np.arange(S) % 20], 1).astype(np.int32)
+    tab = _t(O.rope_table(pos), gpu)
+    hq, hk, hv = (torch.from_numpy(a.view(np.int16)).view(torch.bfloat16).pin_memory() for a in (q, k, v))
+    hout = torch.empty_like(hq).pin_memory()
+    ha = HostAttention(0, H, S, chunk_heads=4)
+    ha(hq, hk, hv, hout, bl.on(gpu), 128 ** -0.5, q_norm=wq, k_norm=wk, eps=1e-6, rope_table=tab)
+    torch.cuda.synchronize()
+    qd, kd, vd = (_t(a, gpu) for a in (q, k, v))
+    want = torch.empty_like(qd)
+    _rt().attn_fwd(q=qd, k=kd, v=vd, out=want, layout="HSD", scale=128 ** -0.5, blocks=bl.on(gpu), q_norm=wq,
+                   k_norm=wk, eps=1e-6, rope_table=tab)
+    torch.cuda.synchronize()
+    assert torch.equal(hout, want.cpu())
