@@ -193,15 +193,17 @@ def test_hsd_layout_and_head_shard(gpu):
     assert np.all(_np(out)[[0, 3]] == 0), "heads outside the shard are untouched"
 
 
-def test_full_size_config2_sampled(gpu):
-    """Config 2 at full size (S=124,992, H=40) on the tcgen05 kernel, checked
-    on a deterministic sample of query blocks and heads."""
+@pytest.mark.parametrize("name,qbs", [("config2", [0, 1, 488, 975, 976]), ("config3", [0, 4, 5, 6, 500, 981])])
+def test_full_size_config2_sampled(gpu, name, qbs):
+    """Configs 2 and 3 at full size (S=124,992 / 125,632, H=40) on the
+    tcgen05 kernel, checked on a deterministic sample of query blocks (for
+    config 3: dense audio rows 0-4 and the first video rows) and heads."""
     import torch
 
     from h3attention import BlockList, Runtime
     from h3attention.configs import CONFIGS
 
-    wl = CONFIGS["config2"]
+    wl = CONFIGS[name]
     S, H = wl.seq_len, wl.heads
     rt = Runtime.get(0)
     q, k, v = (rt.fill_normal(torch.empty((S, H, 128), dtype=torch.bfloat16, device=gpu), wl.seed, st)
@@ -210,7 +212,6 @@ def test_full_size_config2_sampled(gpu):
     out = torch.empty_like(q)
     rt.attn_fwd(q=q, k=k, v=v, out=out, layout="SHD", scale=1 / np.sqrt(128), blocks=bl.on(gpu))
     torch.cuda.synchronize()
-    qbs = [0, 1, 488, 975, 976]
     heads = (17, 19)
     qh, kh, vh = (_np(t[:, heads[0]:heads[1]]) for t in (q, k, v))
     want = O.attend_streaming(qh, kh, vh, bl.row_ptr, bl.col_idx, qblocks=qbs)
