@@ -228,6 +228,33 @@ class CUDABackend(_KernelBackend):
             return None
         return self._run(queries, keys, values, scale, self.blocks)
 
+    def attend_fused(self, queries, keys, values, scale: float, q_norm_weight, k_norm_weight, eps: float,
+                     rope_table, context: AttentionContext):
+        """The optional fused entry: ``queries``/``keys`` are the PRE-norm
+        per-head projections (``[H, S, D]`` views of the QKV GEMM output);
+        RMSNorm (``Modulation.swift:116-120``) and split-half RoPE
+        (``DiTBlock.swift:83-103``) run inside the call, in the order of
+        ``AttentionLayer.callAsFunction`` (``DiTBlock.swift:346-352``).
+        ``rope_table`` is the render's ``[S, half, 4]`` bf16 table or None.
+        Same decline rules as ``attend``."""
+        if self.spec is None or not _check_operands(queries, keys, values):
+            return None
+        S = queries.shape[1]
+        if S != self.spec.seq_len or context.sequence_length != S:
+            return None
+        if S < self.min_sequence_length or context.block_index in self.dense_blocks:
+            return None
+        if context.video_span is not None and context.video_span != (self.spec.prefix_len, S):
+            return None
+        import torch
+
+        out = torch.empty_like(queries)
+        Runtime.get(queries.device.index).attn_fwd(
+            q=queries, k=keys, v=values, out=out, layout="HSD", scale=scale,
+            blocks=self.blocks.on(queries.device), flags=self.kernel_flags, q_norm=q_norm_weight,
+            k_norm=k_norm_weight, eps=eps, rope_table=rope_table)
+        return out
+
 
 class AttentionRegistry:
     """AttentionBackend.swift:188-283."""

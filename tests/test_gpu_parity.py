@@ -245,3 +245,42 @@ def test_host_pipeline_matches_device_call(gpu):
                    k_norm=wk, eps=1e-6, rope_table=tab)
     torch.cuda.synchronize()
     assert torch.equal(hout, want.cpu())
+
+
+def test_backend_seam_fused_and_decline(gpu):
+    """The seam mirror: CUDABackend.attend_fused equals prologue + attend;
+    a call outside the prepared layout is declined (None) and sdpa() then
+    runs the dense path, which equals the backend with every block kept."""
+    import torch
+
+    from h3attention import AttentionContext, AttentionRegistry, Machine, MaskSpec, sdpa
+
+    S, H = 1024, 2
+    sel = AttentionRegistry.resolve("b200-block-sparse", Machine.detect())
+    spec = MaskSpec(seq_len=S, frames=4, height=16, width=16, n_random=1, seed=9)
+    sel.backend.prepare_render(spec)
+    ctx = AttentionContext(block_index=3, block_count=50, schedule_progress=0.5, sequence_length=S,
+                           video_span=(0, S))
+    q, k, v = (O.fill_normal_bf16((H, S, 128), 23, st) for st in (1, 2, 3))
+    wq, wk = (O.fill_normal_bf16((128,), 23, st, 1.0, 0.02) for st in (4, 5))
+    pos = np.stack([np.arange(S) // 256, (np.arange(S) // 16) % 16, np.arange(S) % 16], 1).astype(np.int32)
+    tab = O.rope_table(pos)
+    qd, kd, vd = (_t(a, gpu) for a in (q, k, v))
+    fused = sel.backend.attend_fused(qd, kd, vd, 128 ** -0.5, _t(wq, gpu), _t(wk, gpu), 1e-6, _t(tab, gpu), ctx)
+    qs, ks = (O.prologue(np.ascontiguousarray(a.transpose(1, 0, 2)), w, 1e-6, tab) for a, w in ((q, wq), (k, wk)))
+    unfused = sel.backend.attend(_t(np.ascontiguousarray(qs.transpose(1, 0, 2)), gpu),
+                                 _t(np.ascontiguousarray(ks.transpose(1, 0, 2)), gpu), vd, 128 ** -0.5, None, ctx)
+    torch.cuda.synchronize()
+    d = (fused.float() - unfused.float()).abs()
+    assert d.max().item() <= 2e-2 and d.mean().item() <= 2e-3
+    # decline: a sequence the render was not prepared for
+    other = AttentionContext(3, 50, 0.5, S // 2, None)
+    half = [t[:, : S // 2] for t in (qd, kd, vd)]
+    assert sel.backend.attend(*half, 128 ** -0.5, None, other) is None
+    # sdpa() with a declining call runs the dense path ([S,H,D] in, [S,H*D] out)
+    shd = [t.transpose(0, 1) for t in half]
+    dense = sdpa(*shd, head_dim=128, backend=sel.backend, context=other)
+    assert dense.shape == (S // 2, H * 128)
+    want = O.attend_dense_f64(*(np.ascontiguousarray(a[:, : S // 2].transpose(1, 0, 2)) for a in (q, k, v)))
+    got = dense.float().cpu().numpy().reshape(S // 2, H, 128).transpose(1, 0, 2)
+    assert np.abs(got - want).max() <= 2e-2
