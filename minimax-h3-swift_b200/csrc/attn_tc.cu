@@ -23,9 +23,10 @@
 // Q and K are K-major operands, V is an MN-major operand.
 //
 // Every mbarrier wait is bounded (wall-clock limit via %globaltimer).  On a
-// timeout the waiting thread records H3C_ERR_TIMEOUT in the status word,
-// raises a CTA-wide abort flag, and every role drains to the common exit,
-// where TMEM is freed.
+// timeout the waiting thread records H3C_ERR_TIMEOUT in the launch's status
+// word and raises a CTA-wide abort flag; every role drains to the common
+// exit, where TMEM is freed, and the waits of every other CTA see the status
+// word and stop too.
 #include <cuda.h>
 
 #include <climits>
@@ -90,6 +91,12 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
   while (true) {
     if (mbar_try(bar, parity)) return true;
     if (*abort_flag) return false;
+    // another CTA's wait already gave up: stop instead of timing out again
+    // (one status word per launch, so a systematic stall ends in one limit)
+    if (status && *(volatile int32_t*)status != 0) {
+      *abort_flag = 1;
+      return false;
+    }
     if (globaltimer() - t0 > limit_ns) {
       *abort_flag = 1;
       if (status) atomicExch(status, (int32_t)H3C_ERR_TIMEOUT);
