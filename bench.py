@@ -57,6 +57,12 @@ class ClockSampler:
                  "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
+            # nvidia-smi needs a moment to start: make sure it is sampling
+            # before the timed region begins
+            t0 = time.time()
+            while not self.rows and time.time() - t0 < 5.0 and self.proc.poll() is None:
+                time.sleep(0.02)
+            self.rows.clear()
         except OSError:
             self.proc = None
         return self
@@ -68,6 +74,8 @@ class ClockSampler:
                 self.rows.append(parts)
 
     def __exit__(self, *exc):
+        if self.proc and not self.rows:
+            time.sleep(0.15)  # a region shorter than the sampling period still gets one sample
         if self.proc:
             self.proc.terminate()
             try:
