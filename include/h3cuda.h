@@ -177,6 +177,29 @@ h3c_status h3c_attn_fwd_sync(h3c_ctx* ctx, const h3c_attn_args* args, void* stre
  * No counterpart in the reference: its MLX path has no allocation-free mode. */
 h3c_status h3c_attn_fwd_noalloc(const h3c_attn_args* args, void* stream, char* err, size_t err_len);
 
+/* --- sequence-sharded path (NCCL) ------------------------------------------ */
+/* Multi-GPU layout for the longest sequences (one process per GPU).  The
+ * reference is single-process (batch 1, one device); this is new.  Rank 0
+ * creates an id, the caller shares it out of band, every rank initialises its
+ * context's communicator (NCCL is loaded at this point with dlopen). */
+typedef struct h3c_comm_id {
+  char internal[128];
+} h3c_comm_id;
+h3c_status h3c_comm_unique_id(h3c_comm_id* out);
+h3c_status h3c_comm_init(h3c_ctx* ctx, const h3c_comm_id* id, int nranks, int rank);
+h3c_status h3c_comm_destroy(h3c_ctx* ctx);   /* also done by h3c_destroy */
+/* Each rank passes its token shard: q/k/v/out views of S_r rows, S_r =
+ * ceil(ceil(seq_len / nranks) / 128) * 128, shard r holding tokens
+ * [r*S_r, (r+1)*S_r); seq_len is the GLOBAL valid length; heads divisible
+ * by nranks, head_offset 0, head_count == heads; row_ptr/col_idx and the
+ * rope table describe the whole sequence.  Grouped ncclSend/ncclRecv turn
+ * [S_r, H, D] into [nranks*S_r, H/nranks, D], the fused call runs on this
+ * rank's heads, and the output shard comes back the same way; output rows
+ * past seq_len are unspecified.  All work is enqueued on `stream`.  Replaces
+ * nothing in the reference (AttentionLayer.sdpa is single-device,
+ * Sources/H3Modules/DiTBlock.swift:293-328). */
+h3c_status h3c_attn_fwd_seqshard(h3c_ctx* ctx, const h3c_attn_args* args, void* stream);
+
 /* --- synthetic inputs ------------------------------------------------------ */
 /* Counter-based N(mean, std) bf16 generator; element i is a function of
  * (seed, stream_id, i) only, bit-identical to the CPU checker's generator. */

@@ -158,6 +158,7 @@ h3c_status h3c_init(int device, h3c_ctx** out) {
 
 h3c_status h3c_destroy(h3c_ctx* ctx) {
   if (!ctx) return H3C_ERR_INVALID_ARGUMENT;
+  h3c_comm_destroy(ctx);
   cudaSetDevice(ctx->device);
   if (ctx->workspace) cudaFree(ctx->workspace);
   if (ctx->d_counter) cudaFree(ctx->d_counter);

@@ -15,6 +15,7 @@ struct h3c_ctx {
   cudaDeviceProp prop{};
   void* workspace = nullptr;      // normalised keys/queries of the fused path
   size_t workspace_bytes = 0;
+  void* comm = nullptr;           // h3c_comm_state of the sequence-sharded path
   int64_t* d_counter = nullptr;   // small device scratch: [0] mask builder nnz, [1] kernel status word
 };
 

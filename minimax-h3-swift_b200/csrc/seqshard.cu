@@ -1,0 +1,239 @@
+// Sequence-sharded attention over NCCL (one process per GPU).
+//
+// Each rank holds a contiguous, block-aligned slice of the tokens for every
+// head: [S_r, H, D] with S_r = ceil(ceil(S / P) / 128) * 128.  One grouped
+// send/recv all-to-all per operand turns that into [P * S_r, H / P, D] (every
+// token, this rank's heads), the fused call runs on it, and one all-to-all
+// returns the output slice.  The reference is single-process
+// (FRAGILE_CONTRACTS.md: batch-1, one device), so this layout is new; it is
+// the C-ABI counterpart of h3attention/sharding.py for callers that drive
+// their own ranks (e.g. Swift).
+//
+// NCCL is opened with dlopen when a communicator is first created, reusing a
+// libnccl.so.2 that the process has already loaded (for example PyTorch's),
+// so the library has no link-time NCCL dependency.
+#include <dlfcn.h>
+
+#include <cstring>
+#include <mutex>
+
+#include "common.cuh"
+
+namespace {
+
+// The few NCCL entry points used, with the ABI of nccl.h (2.x).
+typedef int ncclResult_t_;
+typedef void* ncclComm_t_;
+typedef struct {
+  char internal[128];
+} ncclUniqueId_;
+enum { kNcclBfloat16 = 9 };  // ncclBfloat16
+
+struct Nccl {
+  ncclResult_t_ (*GetUniqueId)(ncclUniqueId_*);
+  ncclResult_t_ (*CommInitRank)(ncclComm_t_*, int, ncclUniqueId_, int);
+  ncclResult_t_ (*CommDestroy)(ncclComm_t_);
+  ncclResult_t_ (*GroupStart)();
+  ncclResult_t_ (*GroupEnd)();
+  ncclResult_t_ (*Send)(const void*, size_t, int, int, ncclComm_t_, cudaStream_t);
+  ncclResult_t_ (*Recv)(void*, size_t, int, int, ncclComm_t_, cudaStream_t);
+  const char* (*GetErrorString)(ncclResult_t_);
+  bool ok = false;
+};
+
+Nccl* nccl() {
+  static Nccl n;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_NOLOAD);
+    if (!h) h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_LOCAL);
+    if (!h) return;
+    n.GetUniqueId = (decltype(n.GetUniqueId))dlsym(h, "ncclGetUniqueId");
+    n.CommInitRank = (decltype(n.CommInitRank))dlsym(h, "ncclCommInitRank");
+    n.CommDestroy = (decltype(n.CommDestroy))dlsym(h, "ncclCommDestroy");
+    n.GroupStart = (decltype(n.GroupStart))dlsym(h, "ncclGroupStart");
+    n.GroupEnd = (decltype(n.GroupEnd))dlsym(h, "ncclGroupEnd");
+    n.Send = (decltype(n.Send))dlsym(h, "ncclSend");
+    n.Recv = (decltype(n.Recv))dlsym(h, "ncclRecv");
+    n.GetErrorString = (decltype(n.GetErrorString))dlsym(h, "ncclGetErrorString");
+    n.ok = n.GetUniqueId && n.CommInitRank && n.CommDestroy && n.GroupStart && n.GroupEnd && n.Send && n.Recv &&
+           n.GetErrorString;
+  });
+  return n.ok ? &n : nullptr;
+}
+
+h3c_status fail(h3c_ctx* ctx, h3c_status st, const std::string& msg) {
+  if (ctx) ctx->err = msg;
+  return st;
+}
+
+// [S_r, H, D] strided view <-> [P][S_r][H/P][D] contiguous, 16-byte vectors.
+// dir 0: view -> packed (before sending); dir 1: packed -> view (after receiving).
+__global__ void pack_kernel(uint16_t* __restrict__ view, int64_t tok, int64_t head, uint16_t* __restrict__ packed,
+                            int32_t s_r, int32_t heads, int32_t hp, int dir) {
+  const int64_t n = (int64_t)s_r * heads * 16;  // 16-byte chunks
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const int c = (int)(i & 15);
+    const int64_t rh = i >> 4;
+    const int h = (int)(rh % heads);
+    const int64_t s = rh / heads;
+    const int p = h / hp, hl = h - p * hp;
+    uint4* a = reinterpret_cast<uint4*>(view + s * tok + (int64_t)h * head) + c;
+    uint4* b = reinterpret_cast<uint4*>(packed + (((int64_t)p * s_r + s) * hp + hl) * 128) + c;
+    if (dir == 0) *b = *a;
+    else *a = *b;
+  }
+}
+
+}  // namespace
+
+struct h3c_comm_state {
+  ncclComm_t_ comm = nullptr;
+  int nranks = 0, rank = 0;
+  void* buf = nullptr;
+  size_t buf_bytes = 0;
+};
+
+namespace {
+h3c_comm_state* comm_of(h3c_ctx* ctx) { return reinterpret_cast<h3c_comm_state*>(ctx->comm); }
+}  // namespace
+
+extern "C" {
+
+h3c_status h3c_comm_unique_id(h3c_comm_id* out) {
+  if (!out) return H3C_ERR_INVALID_ARGUMENT;
+  Nccl* n = nccl();
+  if (!n) return H3C_ERR_NCCL;
+  ncclUniqueId_ id;
+  if (n->GetUniqueId(&id) != 0) return H3C_ERR_NCCL;
+  static_assert(sizeof(id) == sizeof(out->internal), "unique id size");
+  std::memcpy(out->internal, id.internal, sizeof(id.internal));
+  return H3C_OK;
+}
+
+h3c_status h3c_comm_init(h3c_ctx* ctx, const h3c_comm_id* id, int nranks, int rank) {
+  if (!ctx) return H3C_ERR_INVALID_ARGUMENT;
+  if (!id || nranks < 1 || rank < 0 || rank >= nranks)
+    return fail(ctx, H3C_ERR_INVALID_ARGUMENT, "h3c_comm_init: bad id/nranks/rank");
+  if (ctx->comm) return fail(ctx, H3C_ERR_INVALID_ARGUMENT, "h3c_comm_init: communicator already initialised");
+  Nccl* n = nccl();
+  if (!n) return fail(ctx, H3C_ERR_NCCL, "h3c_comm_init: libnccl.so.2 could not be loaded");
+  H3_CUDA_TRY(ctx, cudaSetDevice(ctx->device));
+  ncclUniqueId_ uid;
+  std::memcpy(uid.internal, id->internal, sizeof(uid.internal));
+  auto* st = new h3c_comm_state();
+  ncclResult_t_ r = n->CommInitRank(&st->comm, nranks, uid, rank);
+  if (r != 0) {
+    delete st;
+    return fail(ctx, H3C_ERR_NCCL, std::string("ncclCommInitRank: ") + n->GetErrorString(r));
+  }
+  st->nranks = nranks;
+  st->rank = rank;
+  ctx->comm = st;
+  return H3C_OK;
+}
+
+h3c_status h3c_comm_destroy(h3c_ctx* ctx) {
+  if (!ctx) return H3C_ERR_INVALID_ARGUMENT;
+  h3c_comm_state* st = comm_of(ctx);
+  if (!st) return H3C_OK;
+  cudaSetDevice(ctx->device);
+  if (st->buf) cudaFree(st->buf);
+  Nccl* n = nccl();
+  if (n && st->comm) n->CommDestroy(st->comm);
+  delete st;
+  ctx->comm = nullptr;
+  return H3C_OK;
+}
+
+h3c_status h3c_attn_fwd_seqshard(h3c_ctx* ctx, const h3c_attn_args* args, void* stream) {
+  if (!ctx) return H3C_ERR_INVALID_ARGUMENT;
+  h3c_comm_state* st = comm_of(ctx);
+  if (!st) return fail(ctx, H3C_ERR_INVALID_ARGUMENT, "h3c_attn_fwd_seqshard: call h3c_comm_init first");
+  if (!args) return fail(ctx, H3C_ERR_INVALID_ARGUMENT, "h3c_attn_fwd_seqshard: null args");
+  const h3c_attn_args& a = *args;
+  const int P = st->nranks;
+  if (a.head_dim != 128 || a.block != 128) return fail(ctx, H3C_ERR_UNSUPPORTED, "h3c_attn_fwd_seqshard: head_dim/block");
+  if (a.heads <= 0 || a.heads % P || a.head_offset != 0 || a.head_count != a.heads)
+    return fail(ctx, H3C_ERR_UNSUPPORTED,
+                "h3c_attn_fwd_seqshard: all heads (head_offset 0, head_count == heads), heads divisible by ranks");
+  if (a.seq_len <= 0) return fail(ctx, H3C_ERR_INVALID_ARGUMENT, "h3c_attn_fwd_seqshard: seq_len");
+  const h3c_view* vs[4] = {&a.q, &a.k, &a.v, &a.out};
+  for (const h3c_view* v : vs)
+    if (!v->ptr || ((uintptr_t)v->ptr & 15) || v->token_stride <= 0 || v->head_stride <= 0 || (v->token_stride & 7) ||
+        (v->head_stride & 7))
+      return fail(ctx, H3C_ERR_INVALID_ARGUMENT, "h3c_attn_fwd_seqshard: q/k/v/out need 16-byte aligned rows");
+  Nccl* n = nccl();
+  if (!n) return fail(ctx, H3C_ERR_NCCL, "h3c_attn_fwd_seqshard: NCCL unavailable");
+  H3_CUDA_TRY(ctx, cudaSetDevice(ctx->device));
+  cudaStream_t s = (cudaStream_t)stream;
+
+  // shard length: whole 128-token blocks, equal on every rank
+  const int per = (a.seq_len + P - 1) / P;
+  const int s_r = (per + 127) / 128 * 128;
+  const int hp = a.heads / P;
+  const size_t elems = (size_t)s_r * a.heads * 128;  // one operand slice == one exchanged operand
+  const size_t need = 5 * elems * sizeof(uint16_t);  // send buffer + exchanged q, k, v and the output
+  if (st->buf_bytes < need) {
+    if (st->buf) {
+      H3_CUDA_TRY(ctx, cudaStreamSynchronize(s));
+      cudaFree(st->buf);
+      st->buf = nullptr;
+      st->buf_bytes = 0;
+    }
+    H3_CUDA_TRY(ctx, cudaMalloc(&st->buf, need));
+    st->buf_bytes = need;
+  }
+  // layout: [send | q_x | k_x | v_x | o_x]; o_x is packed back through send
+  uint16_t* send = (uint16_t*)st->buf;
+  uint16_t* qx = send + elems;
+  uint16_t* kx = qx + elems;
+  uint16_t* vx = kx + elems;
+  uint16_t* ox = vx + elems;
+  const size_t chunk = (size_t)s_r * hp * 128;  // elements exchanged with one peer
+  const int threads = 256;
+  const int blocks = ctx->prop.multiProcessorCount * 8;
+
+  auto exchange = [&](uint16_t* src, uint16_t* dst) -> h3c_status {
+    if (n->GroupStart() != 0) return fail(ctx, H3C_ERR_NCCL, "ncclGroupStart");
+    for (int p = 0; p < P; ++p) {
+      if (n->Send(src + p * chunk, chunk, kNcclBfloat16, p, st->comm, s) != 0 ||
+          n->Recv(dst + p * chunk, chunk, kNcclBfloat16, p, st->comm, s) != 0) {
+        n->GroupEnd();
+        return fail(ctx, H3C_ERR_NCCL, "ncclSend/ncclRecv");
+      }
+    }
+    if (n->GroupEnd() != 0) return fail(ctx, H3C_ERR_NCCL, "ncclGroupEnd");
+    return H3C_OK;
+  };
+  const h3c_view ins[3] = {a.q, a.k, a.v};
+  uint16_t* outs[3] = {qx, kx, vx};
+  for (int i = 0; i < 3; ++i) {
+    pack_kernel<<<blocks, threads, 0, s>>>((uint16_t*)ins[i].ptr, ins[i].token_stride, ins[i].head_stride, send, s_r,
+                                           a.heads, hp, 0);
+    H3_CUDA_TRY(ctx, cudaGetLastError());
+    h3c_status e = exchange(send, outs[i]);
+    if (e != H3C_OK) return e;
+  }
+  // the fused call on [P * S_r, H/P, D]: every token, this rank's heads
+  h3c_attn_args la = a;
+  const int64_t ts = (int64_t)hp * 128;
+  la.q = h3c_view{qx, ts, 128};
+  la.k = h3c_view{kx, ts, 128};
+  la.v = h3c_view{vx, ts, 128};
+  la.out = h3c_view{ox, ts, 128};
+  la.heads = hp;
+  la.head_offset = 0;
+  la.head_count = hp;
+  h3c_status e = h3c_attn_fwd(ctx, &la, stream);
+  if (e != H3C_OK) return e;
+  // rows past seq_len are not computed; they come back as unspecified padding
+  e = exchange(ox, send);
+  if (e != H3C_OK) return e;
+  pack_kernel<<<blocks, threads, 0, s>>>((uint16_t*)a.out.ptr, a.out.token_stride, a.out.head_stride, send, s_r,
+                                         a.heads, hp, 1);
+  H3_CUDA_TRY(ctx, cudaGetLastError());
+  return H3C_OK;
+}
+
+}  // extern "C"

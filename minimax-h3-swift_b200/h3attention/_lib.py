@@ -37,6 +37,7 @@ EXPORTS = (
     "h3c_device_count", "h3c_blockmask_build", "h3c_blockmask_build_device", "h3c_rope_table",
     "h3c_prologue", "h3c_attn_fwd", "h3c_attn_workspace_size", "h3c_attn_fwd_sync",
     "h3c_fill_normal_bf16", "h3c_attn_fwd_noalloc", "h3c_device_status",
+    "h3c_comm_unique_id", "h3c_comm_init", "h3c_comm_destroy", "h3c_attn_fwd_seqshard",
 )
 
 
@@ -69,6 +70,10 @@ class MaskSpec(C.Structure):
 
 class View(C.Structure):
     _fields_ = [("ptr", C.c_void_p), ("token_stride", C.c_int64), ("head_stride", C.c_int64)]
+
+
+class CommId(C.Structure):
+    _fields_ = [("internal", C.c_char * 128)]
 
 
 class AttnArgs(C.Structure):
@@ -113,6 +118,10 @@ def load() -> C.CDLL:
             "h3c_attn_fwd_sync": ([vp, C.POINTER(AttnArgs), vp], st),
             "h3c_fill_normal_bf16": ([vp, vp, i64, u64, u64, f64, f64, vp], st),
             "h3c_device_status": ([vp], st),
+            "h3c_comm_unique_id": ([C.POINTER(CommId)], st),
+            "h3c_comm_init": ([vp, C.POINTER(CommId), C.c_int, C.c_int], st),
+            "h3c_comm_destroy": ([vp], st),
+            "h3c_attn_fwd_seqshard": ([vp, C.POINTER(AttnArgs), vp], st),
             "h3c_attn_fwd_noalloc": ([C.POINTER(AttnArgs), vp, C.c_char_p, C.c_size_t], st),
         }
         for name, (args, res) in sig.items():

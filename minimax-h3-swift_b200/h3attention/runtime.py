@@ -110,6 +110,27 @@ class Runtime:
         a = self.attn_args(**kw)
         self._check(self.L.h3c_attn_fwd_sync(self.ctx, C.byref(a), _stream_ptr(stream)))
 
+    # ------------------------------------------------- sequence-sharded path
+    @staticmethod
+    def comm_unique_id() -> bytes:
+        cid = _lib.CommId()
+        _lib.check(_lib.load().h3c_comm_unique_id(C.byref(cid)), what="h3c_comm_unique_id")
+        return C.string_at(C.addressof(cid), 128)  # all 128 bytes (the id holds NULs)
+
+    def comm_init(self, unique_id: bytes, nranks: int, rank: int):
+        if len(unique_id) != 128:
+            raise ValueError("an NCCL unique id is 128 bytes")
+        cid = _lib.CommId()
+        C.memmove(C.addressof(cid), unique_id, 128)
+        self._check(self.L.h3c_comm_init(self.ctx, C.byref(cid), nranks, rank))
+
+    def attn_fwd_seqshard(self, *, stream=None, **kw):
+        """This rank's [S_r, H, D] shards in and out; ``seq_len`` is global."""
+        seq_len = kw.pop("seq_len")
+        a = self.attn_args(**kw)
+        a.seq_len = seq_len
+        self._check(self.L.h3c_attn_fwd_seqshard(self.ctx, C.byref(a), _stream_ptr(stream)))
+
     def device_status(self):
         self._check(self.L.h3c_device_status(self.ctx))
 

@@ -48,6 +48,8 @@ def test_no_device_status_on_cpu(lib):
     assert lib.load().h3c_device_count(C.byref(n)) == 0 and n.value == 0
     assert lib.load().h3c_last_error(None) == b"h3c: null context"
     assert lib.load().h3c_attn_fwd(None, None, None) == lib.H3C_ERR_INVALID_ARGUMENT
+    assert lib.load().h3c_attn_fwd_seqshard(None, None, None) == lib.H3C_ERR_INVALID_ARGUMENT
+    assert lib.load().h3c_comm_init(None, None, 2, 0) == lib.H3C_ERR_INVALID_ARGUMENT
 
 
 CASES = [

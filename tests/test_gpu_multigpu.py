@@ -73,3 +73,75 @@ def test_ulysses_two_gpus_matches_single_gpu(gpu):
         assert p.exitcode == 0
     for rank, err in res:
         assert err == 0.0, (rank, err)  # same kernels, same per-head inputs
+
+
+def _abi_worker(rank, world, id_q, q_out):
+    try:
+        _abi_body(rank, world, id_q, q_out)
+    except Exception as e:  # report instead of leaving the parent waiting
+        q_out.put((rank, repr(e)))
+
+
+def _abi_body(rank, world, id_q, q_out):
+    import sys
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    sys.path[:0] = [root, os.path.join(root, "minimax-h3-swift_b200")]
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    import torch
+
+    from h3attention import BlockList, Runtime
+    from h3attention.configs import CONFIGS, EPS
+    from h3attention.sharding import seq_shard_len
+
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    wl = CONFIGS["config1"]
+    S, H = wl.seq_len, wl.heads
+    rt = Runtime.get(rank)
+    if rank == 0:  # rank 0 creates the NCCL id and hands it to the others
+        uid = Runtime.comm_unique_id()
+        for _ in range(world - 1):
+            id_q.put(uid)
+    else:
+        uid = id_q.get(timeout=60)
+    n = seq_shard_len(S, world)
+    full = [rt.fill_normal(torch.empty((n * world, H, 128), dtype=torch.bfloat16, device=dev), 6, st) for st in (1, 2, 3)]
+    wq, wk = (rt.fill_normal(torch.empty(128, dtype=torch.bfloat16, device=dev), 6, st, 1.0, 0.02) for st in (4, 5))
+    tab = rt.rope_table(torch.from_numpy(wl.positions()).to(dev))
+    bl = BlockList.build(wl.mask_spec())
+    rt.comm_init(uid, world, rank)
+    mine = [t[rank * n:(rank + 1) * n].contiguous() for t in full]
+    out = torch.empty_like(mine[0])
+    rt.attn_fwd_seqshard(q=mine[0], k=mine[1], v=mine[2], out=out, layout="SHD", scale=128 ** -0.5,
+                         blocks=bl.on(dev), q_norm=wq, k_norm=wk, eps=EPS, rope_table=tab, seq_len=S)
+    want = torch.empty_like(full[0])
+    rt.attn_fwd(q=full[0][:S], k=full[1][:S], v=full[2][:S], out=want[:S], layout="SHD", scale=128 ** -0.5,
+                blocks=bl.on(dev), q_norm=wq, k_norm=wk, eps=EPS, rope_table=tab)
+    torch.cuda.synchronize()
+    lo, hi = rank * n, min(S, (rank + 1) * n)
+    q_out.put((rank, (out[: hi - lo].float() - want[lo:hi].float()).abs().max().item()))
+
+
+def test_c_abi_seqshard_two_gpus(gpu):
+    """h3c_comm_init + h3c_attn_fwd_seqshard (NCCL grouped send/recv inside
+    the library) on 2 GPUs equals the single-GPU fused call."""
+    import torch
+    import torch.multiprocessing as mp
+
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    ctx = mp.get_context("spawn")
+    q, id_q = ctx.Queue(), ctx.Queue()
+    procs = [ctx.Process(target=_abi_worker, args=(r, 2, id_q, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    try:
+        res = [q.get(timeout=120) for _ in range(2)]
+    finally:
+        for p in procs:
+            p.join(timeout=30)
+            if p.is_alive():
+                p.kill()
+    for rank, err in res:
+        assert err == 0.0, (rank, err)
