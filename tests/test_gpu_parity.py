@@ -284,3 +284,31 @@ def test_backend_seam_fused_and_decline(gpu):
     want = O.attend_dense_f64(*(np.ascontiguousarray(a[:, : S // 2].transpose(1, 0, 2)) for a in (q, k, v)))
     got = dense.float().cpu().numpy().reshape(S // 2, H, 128).transpose(1, 0, 2)
     assert np.abs(got - want).max() <= 2e-2
+
+
+def test_qkv_direct_views(gpu):
+    """q, k, v read straight from one [S, 3*H*D] QKV GEMM output (Q|K|V
+    blocked, head-major inside, DiTBlock.swift:338-344) through strided
+    views, with the fused prologue: equals the call on split copies."""
+    import torch
+
+    from h3attention import BlockList, MaskSpec
+    from h3attention._lib import View
+
+    S, H = 1500, 3
+    qkv = _t(O.fill_normal_bf16((S, 3 * H * 128), 31, 1), gpu)
+    wq, wk = (_t(O.fill_normal_bf16((128,), 31, st, 1.0, 0.02), gpu) for st in (4, 5))
+    pos = np.stack([np.arange(S) // 300, (np.arange(S) // 20) % 15, np.arange(S) % 20], 1).astype(np.int32)
+    tab = _t(O.rope_table(pos), gpu)
+    bl = BlockList.build(MaskSpec(seq_len=S, frames=5, height=15, width=20, n_random=1, seed=2))
+    views = [qkv[:, i * H * 128:(i + 1) * H * 128].view(S, H, 128) for i in range(3)]  # strided, no copy
+    assert views[0].stride() == (3 * H * 128, 128, 1)
+    out_v = torch.empty((S, H, 128), dtype=torch.bfloat16, device=gpu)
+    _rt().attn_fwd(q=views[0], k=views[1], v=views[2], out=out_v, layout="SHD", scale=128 ** -0.5,
+                   blocks=bl.on(gpu), q_norm=wq, k_norm=wk, eps=1e-6, rope_table=tab)
+    copies = [t.contiguous() for t in views]
+    out_c = torch.empty_like(out_v)
+    _rt().attn_fwd(q=copies[0], k=copies[1], v=copies[2], out=out_c, layout="SHD", scale=128 ** -0.5,
+                   blocks=bl.on(gpu), q_norm=wq, k_norm=wk, eps=1e-6, rope_table=tab)
+    torch.cuda.synchronize()
+    assert torch.equal(out_v, out_c)
