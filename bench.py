@@ -134,7 +134,14 @@ class CpuBaseline:
         S, H = wl.seq_len, self.H
         self.order = np.random.default_rng(7).permutation(self.bl.n_blocks)
         self.sizes = np.minimum(128, S - np.arange(self.bl.n_blocks) * 128).astype(np.float64)
-        self.tab = O.rope_table(wl.positions())
+        if wl.render:
+            from h3attention.configs import shared_inv_freq
+
+            text, width, height, length = wl.render
+            _, pos = O.packed_layout(text, O.latent_geometry(width, height, length))
+            self.tab = O.rope_table_shared(pos.astype(np.float32), shared_inv_freq())
+        else:
+            self.tab = O.rope_table(wl.positions())
         self.q, self.k, self.v = (O.fill_normal_bf16((S, H, 128), wl.seed, st) for st in (1, 2, 3))
         self.wq, self.wk = (O.fill_normal_bf16((128,), wl.seed, st, 1.0, 0.02) for st in (4, 5))
         self.cursor = 0
@@ -142,7 +149,7 @@ class CpuBaseline:
     def sample(self, budget_s):
         O, np, bl, wl, H = self.O, self.np, self.bl, self.wl, self.H
         t0 = time.perf_counter()
-        qn, kn = O.prologue(self.q, self.wq, 1e-6, self.tab), O.prologue(self.k, self.wk, 1e-6, self.tab)
+        qn, kn = O.prologue(self.q, self.wq, wl.eps, self.tab), O.prologue(self.k, self.wk, wl.eps, self.tab)
         pro_s = time.perf_counter() - t0
         nb = bl.n_blocks
         step = max(self.threads, 8)
@@ -220,7 +227,7 @@ def run_ours(args):
 
     from h3attention import BlockList, Runtime
     from h3attention.sharding import cuda_attend_fn, head_range, seq_shard_len, ulysses_attend
-    from h3attention.configs import EPS, ROPE_DIMS, ROPE_THETA, STREAM_K, STREAM_Q, STREAM_V, STREAM_WK, STREAM_WQ
+    from h3attention.configs import STREAM_K, STREAM_Q, STREAM_V, STREAM_WK, STREAM_WQ
 
     ws, rank, local = _dist()
     torch.cuda.set_device(local)
@@ -246,7 +253,8 @@ def run_ours(args):
         rows, hl = S, H
     q, k, v = fill((rows, hl, 128), STREAM_Q), fill((rows, hl, 128), STREAM_K), fill((rows, hl, 128), STREAM_V)
     wq, wk = fill((128,), STREAM_WQ, 1.0, 0.02), fill((128,), STREAM_WK, 1.0, 0.02)
-    tab = rt.rope_table(torch.from_numpy(wl.positions()).to(dev), ROPE_DIMS, ROPE_THETA)
+    tab = wl.rope_table(rt, dev)
+    EPS = wl.eps
     bl = BlockList.build(wl.mask_spec())
     blocks = bl.on(dev)
     scale = 128 ** -0.5
@@ -362,7 +370,9 @@ def run_ours(args):
                        "l2": "inputs larger than L2 (no flush)",
                        "parallelism": {"replica": f"replicas x{ws} (weak)", "heads": f"head-sharded x{ws}",
                                        "seq": f"sequence-sharded x{ws} (NCCL all-to-all)"}[mode],
-                       "prologue": "fused RMSNorm + RoPE (t/h/w 32/48/48, theta 1e4)"},
+                       "prologue": (f"fused RMSNorm (eps {EPS:g}) + RoPE from the packed layout (rot 96, shared "
+                                    "inv_freq)" if wl.render else
+                                    f"fused RMSNorm (eps {EPS:g}) + RoPE (t/h/w 32/48/48, theta 1e4)")},
             "e2e": {"value": job_flops / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": e2e_ms,
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
             "roofline": {"bound": "tensor", "kernel": "attn_tc_kernel", "achieved": achieved,
@@ -388,7 +398,7 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--config", default="config2",
-                    help="config1..config4 or config5@<density>; default config2 (the 5 s 1344x768 clip)")
+                    help="config1..config4, config5@<density> or production; default config2 (the 5 s 1344x768 clip)")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--mode", default="replica", choices=["replica", "heads", "seq"],
                     help="N>1 layout: independent full calls per rank (weak), heads split across ranks, or "

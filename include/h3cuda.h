@@ -19,6 +19,16 @@
  *   h3c_rope_table        H3RoPE.angles + rotationTable
  *                         (Sources/H3Modules/H3Transformer.swift:62-78),
  *                         built once per render in prepareRender (:263-276)
+ *   h3c_rope_table_shared the same table as the production transformer builds
+ *                         it: float PackedLayout.positionIds and the
+ *                         checkpoint's shared rope.inv_freq (H3Transformer.
+ *                         swift:62-78, :270-273; PackedSequence.swift:186)
+ *   h3c_packed_layout     PackedLayout.init segment table (Sources/H3Foundation/
+ *                         PackedSequence.swift:192-297), host only
+ *   h3c_packed_positions_device  PackedLayout.positionIds narrowed to fp32
+ *                         (H3Transformer.swift:270), evaluated on the device
+ *   h3c_rope_table_layout positions + H3RoPE table in one kernel: what
+ *                         prepareRender builds (H3Transformer.swift:263-276)
  *   h3c_blockmask_build   new: the compacted 128x128 block list (no reference
  *                         counterpart; prefix rule of AxialTopology.allows,
  *                         Sources/H3Attention/AxialTopology.swift:128-137)
@@ -143,6 +153,54 @@ h3c_status h3c_blockmask_build_device(h3c_ctx* ctx, const h3c_mask_spec* spec, i
  * dims = rotary channels per axis (sum = 2*half), theta as H3RoPE. */
 h3c_status h3c_rope_table(h3c_ctx* ctx, const int32_t* d_pos, int32_t seq_len, const int32_t dims[3],
                           double theta, void* d_table, void* stream);
+/* RoPE table from float positions d_pos [S,3] (t,h,w; fractional values
+ * allowed, as PackedLayout makes them) and ONE shared inverse-frequency
+ * vector d_inv_freq [n] (the checkpoint's rope.inv_freq) applied to each
+ * axis: half = 3n pairs, angle(s, a*n+k) = pos[s,a] * inv[k] in fp32,
+ * entry (c, -s, s, c) rounded to bf16.  All pointers are device memory;
+ * no allocation, no synchronisation (stream-ordered).  3n <= 64. */
+h3c_status h3c_rope_table_shared(h3c_ctx* ctx, const float* d_pos, int32_t seq_len, const float* d_inv_freq,
+                                 int32_t n, void* d_table, void* stream);
+/* --- packed layout (PackedSequence.swift) -------------------------------- */
+/* Segment kinds, in SegmentKind's order (PackedSequence.swift:20-27). */
+enum { H3C_SEG_TEXT = 0, H3C_SEG_COND = 1, H3C_SEG_REF_IMAGE = 2, H3C_SEG_REF_AUDIO = 3, H3C_SEG_AUDIO = 4,
+       H3C_SEG_VIDEO = 5 };
+/* ReferenceKind (PackedSequence.swift:157-162). */
+enum { H3C_REF_IMAGE = 0, H3C_REF_AUDIO = 1, H3C_REF_VIDEO = 2, H3C_REF_VIDEO_AUDIO = 3 };
+
+typedef struct {          /* ReferenceBlock */
+  int32_t kind, latent_h, latent_w, latent_t, ref_audio_t;
+} h3c_ref_block;
+
+typedef struct {          /* PackedLayout(textTokens:geometry:keyframes:refs:) */
+  int32_t text_tokens;
+  int32_t frame_count, latent_t, audio_t, latent_h, latent_w;  /* LatentGeometry */
+  int32_t patch;                      /* H3Config.patchSize[1] (2) */
+  int32_t n_keyframes;
+  const int32_t* keyframes;           /* resolved pixel frame indices */
+  int32_t n_refs;
+  const h3c_ref_block* refs;
+} h3c_layout_spec;
+
+typedef struct { int32_t start, stop, kind; } h3c_segment;
+
+/* Segment table and total rows of the packed sequence (host only).  An
+ * anchor off the timeline or an axis smaller than the patch is refused with
+ * H3C_ERR_INVALID_ARGUMENT (the reference throws H3Error there).  capacity 0
+ * queries the counts; a smaller non-zero capacity returns H3C_ERR_CAPACITY. */
+h3c_status h3c_packed_layout(const h3c_layout_spec* spec, h3c_segment* segments, int32_t capacity,
+                             int32_t* n_segments, int64_t* total_tokens);
+/* d_pos [S, 3] fp32 = Float(positionIds), bit-identical to the reference's
+ * float64 construction narrowed to fp32.  capacity in tokens.  At most 40
+ * segments.  Stream-ordered, no allocation. */
+h3c_status h3c_packed_positions_device(h3c_ctx* ctx, const h3c_layout_spec* spec, float* d_pos, int64_t capacity,
+                                       void* stream);
+/* d_table [S, 3n, 4] bf16 from the layout's positions and the shared
+ * d_inv_freq [n] (equal to h3c_packed_positions_device followed by
+ * h3c_rope_table_shared, without the positions buffer). */
+h3c_status h3c_rope_table_layout(h3c_ctx* ctx, const h3c_layout_spec* spec, const float* d_inv_freq, int32_t n,
+                                 void* d_table, int64_t capacity, void* stream);
+
 /* out = SplitHalfRoPE(RMSNorm(x)) for one operand (q or k), rows (s, h) for
  * h in [head_offset, head_offset+head_count).  table NULL: RMSNorm only. */
 h3c_status h3c_prologue(h3c_ctx* ctx, h3c_view x, h3c_view out, int32_t seq_len, int32_t heads,

@@ -12,6 +12,8 @@
 namespace h3 {
 cudaError_t launch_rope_table(const int32_t* pos, int32_t seq_len, int3 dims, const float* d_inv, int32_t half,
                               uint16_t* table, cudaStream_t s);
+cudaError_t launch_rope_table_shared(const float* pos, int32_t seq_len, const float* d_inv, int32_t n,
+                                     uint16_t* table, cudaStream_t s);
 cudaError_t launch_mask_build(const h3c_mask_spec& sp, int32_t* counts, int32_t* row_ptr, int32_t* col_idx,
                               int64_t capacity, int64_t* d_nnz, cudaStream_t s);
 cudaError_t launch_fill_normal(uint16_t* out, int64_t n, uint64_t seed, uint64_t stream, double mean, double std,
@@ -276,6 +278,18 @@ h3c_status h3c_rope_table(h3c_ctx* ctx, const int32_t* d_pos, int32_t seq_len, c
   cudaFreeAsync(d_inv, s);
   H3_CUDA_TRY(ctx, e);
   H3_CUDA_TRY(ctx, e2);
+  return H3C_OK;
+}
+
+h3c_status h3c_rope_table_shared(h3c_ctx* ctx, const float* d_pos, int32_t seq_len, const float* d_inv_freq,
+                                 int32_t n, void* d_table, void* stream) {
+  if (!ctx) return H3C_ERR_INVALID_ARGUMENT;
+  if (!d_pos || !d_inv_freq || !d_table || seq_len < 0 || n <= 0)
+    return fail(ctx, H3C_ERR_INVALID_ARGUMENT, "h3c_rope_table_shared: invalid argument");
+  if (3 * n > 64) return fail(ctx, H3C_ERR_UNSUPPORTED, "h3c_rope_table_shared: 3*n must be <= 64");
+  H3_CUDA_TRY(ctx, cudaSetDevice(ctx->device));
+  H3_CUDA_TRY(ctx, h3::launch_rope_table_shared(d_pos, seq_len, d_inv_freq, n, (uint16_t*)d_table,
+                                                (cudaStream_t)stream));
   return H3C_OK;
 }
 

@@ -79,11 +79,13 @@ __global__ void __launch_bounds__(256) prologue_kernel(const uint16_t* __restric
   *reinterpret_cast<uint4*>(y + s * y_tok + h * y_head + 8 * t) = make_uint4(o[0], o[1], o[2], o[3]);
 }
 
-// Specialisation for half == 64 (rot == head_dim, the benchmark's RoPE) and
-// for RMSNorm alone: thread t of 16 owns the rotation pairs 4t..4t+3, i.e.
-// channels 4t..4t+3 and 64+4t..64+4t+3, so each pair and its table entries
-// stay in registers.  Same arithmetic as prologue_kernel, with the rotation
-// on packed bf16x2 operations.
+// Specialisation for any half that is a multiple of 4 (the benchmark's
+// half 64, the production model's half 48) and for RMSNorm alone.  Every
+// thread of the 16 on a row holds 8 channels: thread t < half/4 owns the
+// rotation pairs 4t..4t+3 (channels 4t..4t+3 and half+4t..half+4t+3), the
+// other threads own 8 contiguous pass-through channels from 2*half up, so
+// each pair and its table entries stay in registers.  Same arithmetic as
+// prologue_kernel, with the rotation on packed bf16x2 operations.
 
 __device__ __forceinline__ void unpack4(uint2 u, float* f) {
   f[0] = __uint_as_float(u.x << 16);
@@ -97,17 +99,21 @@ __global__ void __launch_bounds__(256) prologue_pairs_kernel(const uint16_t* __r
                                                              int64_t x_head, uint16_t* __restrict__ y, int64_t y_tok,
                                                              int64_t y_head, int32_t seq_len, int32_t head_count,
                                                              const uint16_t* __restrict__ w, float eps,
-                                                             const uint16_t* __restrict__ table) {
+                                                             const uint16_t* __restrict__ table, int32_t half) {
   const int sub = threadIdx.x >> 4, t = threadIdx.x & 15;
   const int64_t row = (int64_t)blockIdx.x * 16 + sub;
   const bool live = row < (int64_t)seq_len * head_count;
   const int64_t s = live ? row / head_count : 0, h = live ? row % head_count : 0;
+  const bool pair = 4 * t < half;
+  // channel offsets of this thread's two groups of 4
+  const int ca = pair ? 4 * t : 2 * half + 8 * (t - half / 4);
+  const int cb = pair ? half + 4 * t : ca + 4;
   float a[4], b[4], wa[4], wb[4];
   float ss = 0.f;
   const uint16_t* xr = x + s * x_tok + h * x_head;
   if (live) {
-    unpack4(*reinterpret_cast<const uint2*>(xr + 4 * t), a);
-    unpack4(*reinterpret_cast<const uint2*>(xr + 64 + 4 * t), b);
+    unpack4(*reinterpret_cast<const uint2*>(xr + ca), a);
+    unpack4(*reinterpret_cast<const uint2*>(xr + cb), b);
 #pragma unroll
     for (int i = 0; i < 4; ++i) ss += a[i] * a[i] + b[i] * b[i];
   }
@@ -115,22 +121,22 @@ __global__ void __launch_bounds__(256) prologue_pairs_kernel(const uint16_t* __r
   for (int o = 8; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffff, ss, o);
   if (!live) return;
   const float inv = 1.0f / sqrtf(ss / 128.f + eps);
-  unpack4(*reinterpret_cast<const uint2*>(w + 4 * t), wa);
-  unpack4(*reinterpret_cast<const uint2*>(w + 64 + 4 * t), wb);
-  // normalised pairs as bf16x2 words: A[k] = channels 4t+2k, 4t+2k+1;
-  // B[k] = the partners 64 channels up
+  unpack4(*reinterpret_cast<const uint2*>(w + ca), wa);
+  unpack4(*reinterpret_cast<const uint2*>(w + cb), wb);
+  // normalised values as bf16x2 words: A[k] = channels ca+2k, ca+2k+1;
+  // B[k] = channels cb+2k, cb+2k+1 (the rotation partners of A[k] on a pair thread)
   __nv_bfloat162 A[2], B[2];
 #pragma unroll
   for (int k = 0; k < 2; ++k) {
     A[k] = __floats2bfloat162_rn((a[2 * k] * inv) * wa[2 * k], (a[2 * k + 1] * inv) * wa[2 * k + 1]);
     B[k] = __floats2bfloat162_rn((b[2 * k] * inv) * wb[2 * k], (b[2 * k + 1] * inv) * wb[2 * k + 1]);
   }
-  if (table) {
+  if (table && pair) {
     // Each product and each sum rounded to bf16 once: bf16 x bf16 is exact
     // in fp32, and where fp32 would round a sum of two bf16 values the bf16
     // result is the larger operand either way, so the packed bf16 ops (no
     // contraction) equal the fp32-then-round steps of the reference.
-    const uint4* tp = reinterpret_cast<const uint4*>(table + (s * 64 + 4 * t) * 4);
+    const uint4* tp = reinterpret_cast<const uint4*>(table + (s * half + 4 * t) * 4);
 #pragma unroll
     for (int k = 0; k < 2; ++k) {
       const uint4 e = tp[k];  // entries 4t+2k and 4t+2k+1: (c, -s, s, c) each
@@ -147,9 +153,9 @@ __global__ void __launch_bounds__(256) prologue_pairs_kernel(const uint16_t* __r
     }
   }
   uint16_t* yr = y + s * y_tok + h * y_head;
-  *reinterpret_cast<uint2*>(yr + 4 * t) =
+  *reinterpret_cast<uint2*>(yr + ca) =
       make_uint2(*reinterpret_cast<uint32_t*>(&A[0]), *reinterpret_cast<uint32_t*>(&A[1]));
-  *reinterpret_cast<uint2*>(yr + 64 + 4 * t) =
+  *reinterpret_cast<uint2*>(yr + cb) =
       make_uint2(*reinterpret_cast<uint32_t*>(&B[0]), *reinterpret_cast<uint32_t*>(&B[1]));
 }
 
@@ -166,6 +172,25 @@ __global__ void rope_table_kernel(const int32_t* __restrict__ pos, int32_t seq_l
   int axis = i < dims.x / 2 ? 0 : (i < (dims.x + dims.y) / 2 ? 1 : 2);
   float p = (float)pos[s * 3 + axis];
   float ang = __fmul_rn(p, inv[i]);
+  float c = (float)cos((double)ang), sn = (float)sin((double)ang);
+  uint16_t* t = table + idx * 4;
+  t[0] = f2bf(c);
+  t[1] = f2bf(-sn);
+  t[2] = f2bf(sn);
+  t[3] = f2bf(c);
+}
+
+// Production table: float positions, one inv_freq vector shared by the
+// three axes (H3RoPE.angles, Sources/H3Modules/H3Transformer.swift:62-68).
+__global__ void rope_table_shared_kernel(const float* __restrict__ pos, int32_t seq_len,
+                                         const float* __restrict__ inv, int32_t n, uint16_t* __restrict__ table) {
+  const int32_t half = 3 * n;
+  int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= (int64_t)seq_len * half) return;
+  int64_t s = idx / half;
+  int i = (int)(idx % half);
+  int axis = i / n;
+  float ang = __fmul_rn(pos[s * 3 + axis], inv[i - axis * n]);
   float c = (float)cos((double)ang), sn = (float)sin((double)ang);
   uint16_t* t = table + idx * 4;
   t[0] = f2bf(c);
@@ -309,9 +334,11 @@ cudaError_t launch_prologue(const uint16_t* x, int64_t x_tok, int64_t x_head, ui
                             const uint16_t* table, int32_t half, cudaStream_t s) {
   int64_t rows = (int64_t)seq_len * head_count;
   if (rows == 0) return cudaSuccess;
-  if (table == nullptr || half == 64) {
+  // the register-pair kernel reads table entries 16 bytes at a time
+  if (table == nullptr || (half % 4 == 0 && ((uintptr_t)table & 15) == 0)) {
     prologue_pairs_kernel<<<(unsigned)((rows + 15) / 16), 256, 0, s>>>(x, x_tok, x_head, y, y_tok, y_head, seq_len,
-                                                                        head_count, w, eps, table);
+                                                                        head_count, w, eps, table,
+                                                                        table ? half : 64);
     return cudaGetLastError();
   }
   prologue_kernel<<<(unsigned)((rows + 15) / 16), 256, 0, s>>>(x, x_tok, x_head, y, y_tok, y_head, seq_len,
@@ -324,6 +351,14 @@ cudaError_t launch_rope_table(const int32_t* pos, int32_t seq_len, int3 dims, co
   int64_t n = (int64_t)seq_len * half;
   if (n == 0) return cudaSuccess;
   rope_table_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(pos, seq_len, dims, d_inv, half, table);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_rope_table_shared(const float* pos, int32_t seq_len, const float* d_inv, int32_t n,
+                                     uint16_t* table, cudaStream_t s) {
+  int64_t total = (int64_t)seq_len * 3 * n;
+  if (total == 0) return cudaSuccess;
+  rope_table_shared_kernel<<<(unsigned)((total + 255) / 256), 256, 0, s>>>(pos, seq_len, d_inv, n, table);
   return cudaGetLastError();
 }
 

@@ -35,6 +35,7 @@ H3C_NO_ROPE = 4
 EXPORTS = (
     "h3c_abi_version", "h3c_init", "h3c_destroy", "h3c_last_error", "h3c_device_info",
     "h3c_device_count", "h3c_blockmask_build", "h3c_blockmask_build_device", "h3c_rope_table",
+    "h3c_rope_table_shared", "h3c_packed_layout", "h3c_packed_positions_device", "h3c_rope_table_layout",
     "h3c_prologue", "h3c_attn_fwd", "h3c_attn_workspace_size", "h3c_attn_fwd_sync",
     "h3c_fill_normal_bf16", "h3c_attn_fwd_noalloc", "h3c_device_status",
     "h3c_comm_unique_id", "h3c_comm_init", "h3c_comm_destroy", "h3c_attn_fwd_seqshard",
@@ -70,6 +71,24 @@ class MaskSpec(C.Structure):
 
 class View(C.Structure):
     _fields_ = [("ptr", C.c_void_p), ("token_stride", C.c_int64), ("head_stride", C.c_int64)]
+
+
+class RefBlock(C.Structure):
+    _fields_ = [("kind", C.c_int32), ("latent_h", C.c_int32), ("latent_w", C.c_int32), ("latent_t", C.c_int32),
+                ("ref_audio_t", C.c_int32)]
+
+
+class LayoutSpec(C.Structure):
+    _fields_ = [
+        ("text_tokens", C.c_int32), ("frame_count", C.c_int32), ("latent_t", C.c_int32), ("audio_t", C.c_int32),
+        ("latent_h", C.c_int32), ("latent_w", C.c_int32), ("patch", C.c_int32),
+        ("n_keyframes", C.c_int32), ("keyframes", C.POINTER(C.c_int32)),
+        ("n_refs", C.c_int32), ("refs", C.POINTER(RefBlock)),
+    ]
+
+
+class Segment(C.Structure):
+    _fields_ = [("start", C.c_int32), ("stop", C.c_int32), ("kind", C.c_int32)]
 
 
 class CommId(C.Structure):
@@ -112,6 +131,10 @@ def load() -> C.CDLL:
             "h3c_blockmask_build": ([C.POINTER(MaskSpec), vp, vp, i64, C.POINTER(i64)], st),
             "h3c_blockmask_build_device": ([vp, C.POINTER(MaskSpec), vp, vp, i64, C.POINTER(i64), vp], st),
             "h3c_rope_table": ([vp, vp, i32, C.POINTER(i32), f64, vp, vp], st),
+            "h3c_rope_table_shared": ([vp, vp, i32, vp, i32, vp, vp], st),
+            "h3c_packed_layout": ([C.POINTER(LayoutSpec), C.POINTER(Segment), i32, C.POINTER(i32), C.POINTER(i64)], st),
+            "h3c_packed_positions_device": ([vp, C.POINTER(LayoutSpec), vp, i64, vp], st),
+            "h3c_rope_table_layout": ([vp, C.POINTER(LayoutSpec), vp, i32, vp, i64, vp], st),
             "h3c_prologue": ([vp, View, View, i32, i32, i32, i32, vp, f32, vp, i32, vp], st),
             "h3c_attn_fwd": ([vp, C.POINTER(AttnArgs), vp], st),
             "h3c_attn_workspace_size": ([C.POINTER(AttnArgs), C.POINTER(C.c_size_t)], st),

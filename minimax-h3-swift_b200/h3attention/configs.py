@@ -8,7 +8,7 @@ dims 32/48/48 (64 rotated pairs, so rot == head_dim).
 from __future__ import annotations
 
 from dataclasses import dataclass, replace
-from typing import Optional
+from typing import Optional, Tuple
 
 import numpy as np
 
@@ -38,6 +38,11 @@ class Workload:
     dense: bool = False
     seed: int = 20260101
     target_density: Optional[float] = None
+    eps: float = EPS
+    # (text_tokens, width, height, length): positions and RoPE table of the
+    # production model, from the packed layout of that render and a shared
+    # 16-entry inv_freq (rot 96); None: the benchmark's integer grid table
+    render: Optional[Tuple[int, int, int, int]] = None
 
     @property
     def video_tokens(self) -> int:
@@ -63,6 +68,26 @@ class Workload:
             vid = np.concatenate([aud, vid], axis=0)
         return np.ascontiguousarray(vid, dtype=np.int32)
 
+    @property
+    def rope_half(self) -> int:
+        return 3 * len(shared_inv_freq()) if self.render else sum(ROPE_DIMS) // 2
+
+    def packed_layout(self):
+        from .layout import LatentGeometry, PackedLayout
+
+        text, width, height, length = self.render
+        return PackedLayout(text, LatentGeometry.make(width, height, length))
+
+    def rope_table(self, runtime, device):
+        """bf16 [S, rope_half, 4] table on ``device``."""
+        import torch
+
+        if self.render:
+            lay = self.packed_layout()
+            assert lay.total_tokens == self.seq_len, (lay.total_tokens, self.seq_len)
+            return lay.rope_table(torch.from_numpy(shared_inv_freq()), torch.device(device).index or 0)
+        return runtime.rope_table(torch.from_numpy(self.positions()).to(device), ROPE_DIMS, ROPE_THETA)
+
     def scaled(self, frames: int, height: int, width: int, heads: Optional[int] = None) -> "Workload":
         return replace(self, frames=frames, height=height, width=width, heads=heads or self.heads)
 
@@ -78,6 +103,20 @@ CONFIGS = {
     # 4: dense roofline, 32^3
     "config4": Workload("config4", heads=40, frames=32, height=32, width=32, dense=True),
 }
+
+
+def shared_inv_freq(n: int = 16, theta: float = ROPE_THETA) -> np.ndarray:
+    """Stand-in for the checkpoint's ``rope.inv_freq`` [16] (no checkpoint
+    here): theta^(-k/16), fp32."""
+    return (theta ** (-np.arange(n, dtype=np.float64) / n)).astype(np.float32)
+
+
+# The production model's own call: 480x864, 5 s (124 frames: 37 latent
+# frames of 15 x 27 tokens), 332 text tokens + 414 audio rows before the
+# video, 56 heads, all blocks kept (the reference runs dense SDPA here),
+# eps 1e-5 (H3Config.swift:32), RoPE from the packed layout (rot 96).
+CONFIGS["production"] = Workload("production", heads=56, frames=37, height=15, width=27, audio=746, dense=True,
+                                 eps=1e-5, render=(332, 864, 480, 120))
 
 
 def config5(density: float) -> Workload:

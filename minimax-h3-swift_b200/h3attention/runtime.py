@@ -158,6 +158,19 @@ class Runtime:
                                           _stream_ptr(stream)))
         return out
 
+    def rope_table_shared(self, pos, inv_freq, stream=None):
+        """The production table: float positions [S, 3] and the shared
+        inv_freq [n] (both fp32 on this device); returns bf16 [S, 3n, 4]."""
+        import torch
+
+        pos = pos.to(torch.float32).contiguous()
+        inv = inv_freq.to(device=pos.device, dtype=torch.float32).contiguous()
+        S, n = pos.shape[0], inv.shape[0]
+        out = torch.empty((S, 3 * n, 4), dtype=torch.bfloat16, device=pos.device)
+        self._check(self.L.h3c_rope_table_shared(self.ctx, pos.data_ptr(), S, inv.data_ptr(), n, out.data_ptr(),
+                                                 _stream_ptr(stream)))
+        return out
+
     def fill_normal(self, out, seed, stream_id, mean=0.0, std=1.0, stream=None):
         self._check(self.L.h3c_fill_normal_bf16(self.ctx, out.data_ptr(), out.numel(), seed, stream_id, mean, std,
                                                 _stream_ptr(stream)))

@@ -433,3 +433,27 @@ void h3o_set_num_threads(int n) {
   (void)n;
 #endif
 }
+
+/* H3RoPE exactly as the reference builds it for the production model
+ * (Sources/H3Modules/H3Transformer.swift:62-78): float positions pos[S,3]
+ * (PackedLayout.positionIds, f64 cast to fp32), ONE shared inv_freq[n]
+ * (from the checkpoint) applied to each of t, h, w; angles =
+ * cat(t*inv, h*inv, w*inv) in fp32 (half = 3n); table entry =
+ * (c, -s, s, c) of fp32 cos/sin (evaluated in double here) rounded to bf16. */
+void h3o_rope_table_shared(const float* pos, int32_t seq_len, const float* inv, int32_t n, uint16_t* table) {
+  const int32_t half = 3 * n;
+#pragma omp parallel for schedule(static)
+  for (int64_t s = 0; s < seq_len; ++s) {
+    for (int a = 0; a < 3; ++a) {
+      for (int k = 0; k < n; ++k) {
+        float ang = pos[s * 3 + a] * inv[k];
+        float c = (float)cos((double)ang), sn = (float)sin((double)ang);
+        uint16_t* t = table + (s * half + a * n + k) * 4;
+        t[0] = f2bf(c);
+        t[1] = f2bf(-sn);
+        t[2] = f2bf(sn);
+        t[3] = f2bf(c);
+      }
+    }
+  }
+}

@@ -63,6 +63,7 @@ def lib():
         L.h3o_rmsnorm_rows.argtypes = [vp, i64, i64, vp, i64, i64, vp, i32, i32, i32, f32]
         L.h3o_rope_rows.argtypes = [vp, i64, i64, vp, i32, i32, i32]
         L.h3o_rope_table.argtypes = [vp, i32, vp, f64, vp]
+        L.h3o_rope_table_shared.argtypes = [vp, i32, vp, i32, vp]
         L.h3o_blockmask_build.argtypes = [C.POINTER(MaskSpec), vp, vp, C.POINTER(C.c_int64)]
         L.h3o_blockmask_build.restype = C.c_int
         L.h3o_blockmask_check.argtypes = [C.POINTER(MaskSpec)]
@@ -138,6 +139,159 @@ def rope_table(pos: np.ndarray, dims=(32, 48, 48), theta: float = 1e4) -> np.nda
     t = np.empty((S, half, 4), dtype=np.uint16)
     lib().h3o_rope_table(_p(pos), S, _p(d), theta, _p(t))
     return t
+
+
+def rope_table_shared(pos: np.ndarray, inv_freq: np.ndarray) -> np.ndarray:
+    """The production H3RoPE (H3Transformer.swift:62-78): float positions
+    [S,3], one shared inv_freq [n] for all three axes; half = 3n."""
+    pos = np.ascontiguousarray(pos, dtype=np.float32)
+    inv = np.ascontiguousarray(inv_freq, dtype=np.float32)
+    S, n = pos.shape[0], inv.shape[0]
+    t = np.empty((S, 3 * n, 4), dtype=np.uint16)
+    lib().h3o_rope_table_shared(_p(pos), S, _p(inv), n, _p(t))
+    return t
+
+
+# ------------------------------------------------------------ packed layout
+# Pure-Python restatement of the position ids of the packed sequence, in
+# float64 like the reference (Python floats are IEEE doubles and never
+# contract into FMA, so every value is the reference's to the last bit).
+
+FPS, LATENT_FPS, LATTICE, LATTICE_OFFSET, SPATIAL_DOWNSAMPLE = 24, 40, 17, 5, 16  # H3Config.swift:59-80
+FRAMES_PER_TOKEN = (1, 4, 4, 4, 4)   # PackedSequence.swift:63
+FRAME_RESCALE = 5.0 / 3.0            # PackedSequence.swift:65
+
+
+class LayoutError(ValueError):
+    """What the reference throws as H3Error (keyframeIndex, dimensionOffGrid)."""
+
+
+def align_frame_count(length: int) -> int:
+    """LatentGeometry.alignFrameCount (LatentGeometry.swift:21-25)."""
+    import math
+    n = max(LATTICE_OFFSET, length)
+    k = int(math.ceil(float(n - LATTICE_OFFSET) / float(LATTICE)))
+    return LATTICE_OFFSET + k * LATTICE
+
+
+def latent_geometry(width: int, height: int, length: int) -> dict:
+    """LatentGeometry.init (LatentGeometry.swift:29-37); Swift's rounded()
+    is half away from zero."""
+    import math
+    f = align_frame_count(length)
+    x = float(f) / float(FPS) * float(LATENT_FPS)
+    audio_t = int(math.floor(x + 0.5))
+    return dict(frame_count=f, latent_t=5 * (f - LATTICE_OFFSET) // LATTICE + 2, audio_t=audio_t,
+                latent_h=height // SPATIAL_DOWNSAMPLE, latent_w=width // SPATIAL_DOWNSAMPLE, patch=2)
+
+
+def position_axis(dim: int, patch: int, sqrt_area: float):
+    """PositionGrid.axis (PackedSequence.swift:69-78)."""
+    ratio = float(dim) / sqrt_area
+    n = dim // patch
+    if n <= 0:
+        raise LayoutError(f"dimension {dim} off the patch grid {patch}")
+    step = ratio / float(n)
+    origin = (1.0 - ratio) / 2.0
+    return [(float(i) * step + origin) * 32.0 for i in range(n)]
+
+
+def frame_grid(h: int, w: int, patch: int = 2):
+    """PositionGrid.frameGrid (PackedSequence.swift:82-92)."""
+    import math
+    area = math.sqrt(float(h) * float(w))
+    ha, wa = position_axis(h, patch, area), position_axis(w, patch, area)
+    return [(hv, wv) for hv in ha for wv in wa], wa
+
+
+def video_t_grid(n: int, origin: float):
+    """PositionGrid.videoTGrid (PackedSequence.swift:95-103)."""
+    out, acc = [], origin
+    for k in range(n):
+        out.append(acc)
+        acc += FRAME_RESCALE * float(FRAMES_PER_TOKEN[k % 5])
+    return out
+
+
+def video_t_span(n: int) -> float:
+    """PositionGrid.videoTSpan (PackedSequence.swift:107-109)."""
+    acc = 0.0
+    for k in range(n):
+        acc = acc + FRAME_RESCALE * float(FRAMES_PER_TOKEN[k % 5])
+    return acc
+
+
+def cond_t(text_tokens: int, latent_t: int, frame_count: int, p: int) -> float:
+    """PositionGrid.condT (PackedSequence.swift:137-142)."""
+    if p == 0:
+        return float(text_tokens)
+    if p == frame_count - 1:
+        return float(text_tokens) + video_t_span(latent_t) - FRAME_RESCALE
+    return float(text_tokens) + FRAME_RESCALE * float(p)
+
+
+SEG_KINDS = ("text", "cond", "ref_img", "ref_audio", "audio", "video")   # SegmentKind order
+
+
+def packed_layout(text_tokens: int, geometry: dict, keyframes=(), refs=()):
+    """PackedLayout.init (PackedSequence.swift:192-297).  ``refs`` entries are
+    dicts with kind in (image, audio, video, video_audio), latent_h, latent_w,
+    latent_t, ref_audio_t.  Returns (segments [(start, stop, kind)], positions
+    as a float64 array [S, 3])."""
+    g = geometry
+    patch = g.get("patch", 2)
+    frame, w_axis = frame_grid(g["latent_h"], g["latent_w"], patch)
+    w_low, w_high = w_axis[0], w_axis[-1]
+    pos, segs, row = [], [], 0
+
+    def seg(n, kind):
+        nonlocal row
+        segs.append((row, row + n, kind))
+        row += n
+
+    seg(text_tokens, "text")
+    pos += [(float(i), 0.0, 0.0) for i in range(text_tokens)]
+    cursor = float(text_tokens)
+    for p in keyframes:
+        if p < 0 or p >= g["frame_count"]:
+            raise LayoutError(f"keyframe {p} off the timeline of {g['frame_count']} frames")
+        ct = cond_t(text_tokens, g["latent_t"], g["frame_count"], p)
+        seg(len(frame), "cond")
+        pos += [(ct, h, w) for h, w in frame]
+    for b in refs:
+        kind = b["kind"]
+        if kind == "image":
+            rf, _ = frame_grid(b["latent_h"], b["latent_w"], patch)
+            seg(len(rf), "ref_img")
+            pos += [(cursor, h, w) for h, w in rf]
+            cursor += 1.0
+        elif kind == "audio":
+            rt = b.get("ref_audio_t", 0)
+            if rt > 0:
+                seg(2 * rt, "ref_audio")
+                for w in (w_low, w_high):
+                    pos += [(cursor + float(i), 0.0, w) for i in range(rt)]
+            cursor += float(rt)
+        elif kind in ("video", "video_audio"):
+            rt, vt = b.get("ref_audio_t", 0), b["latent_t"]
+            rf, rw = frame_grid(b["latent_h"], b["latent_w"], patch)
+            if rt > 0:
+                seg(2 * rt, "ref_audio")
+                for w in (rw[0], rw[-1]):
+                    pos += [(cursor + float(i), 0.0, w) for i in range(rt)]
+            seg(vt * len(rf), "ref_img")
+            for t in video_t_grid(vt, cursor):
+                pos += [(t, h, w) for h, w in rf]
+            cursor += max(float(rt), video_t_span(vt))
+        else:
+            raise LayoutError(f"unknown reference kind {kind}")
+    seg(2 * g["audio_t"], "audio")
+    for w in (w_low, w_high):
+        pos += [(cursor + float(i), 0.0, w) for i in range(g["audio_t"])]
+    seg(g["latent_t"] * len(frame), "video")
+    for t in video_t_grid(g["latent_t"], cursor):
+        pos += [(t, h, w) for h, w in frame]
+    return segs, np.array(pos, dtype=np.float64).reshape(-1, 3)
 
 
 # ----------------------------------------------------------------- block mask

@@ -35,6 +35,8 @@ def test_struct_layout_matches_header(lib):
     assert C.sizeof(lib.MaskSpec) == 13 * 4 + 4 + 8
     assert C.sizeof(lib.View) == 24
     assert C.sizeof(lib.DevInfo) == 4 * 4 + 16 + 4 * 4 + 96
+    assert C.sizeof(lib.RefBlock) == 20 and C.sizeof(lib.Segment) == 12
+    assert C.sizeof(lib.LayoutSpec) == 8 * 4 + 8 + 8 + 8
 
 
 def test_no_device_status_on_cpu(lib):

@@ -1,0 +1,90 @@
+"""Device position ids and the production RoPE table vs the checker, and the
+fused call run the way the production model runs it (B200 only).
+
+Positions are bit-exact (fp32 narrowing of the same float64 operations).
+Table entries: at most one bf16 ulp on a handful of entries (the device's
+double cos/sin vs the host libm, both rounded to fp32 then bf16), as for
+the benchmark's table.  Attention: max-abs <= 2e-2, mean-abs <= 2e-3."""
+import numpy as np
+import pytest
+
+from oracle import oracle as O
+
+from test_layout import LAYOUT_CASES, REF_SETS, _library_layout
+
+pytestmark = pytest.mark.gpu
+
+
+def _inv_freq(n=16, theta=1e4):
+    return (theta ** (-np.arange(n, dtype=np.float64) / n)).astype(np.float32)
+
+
+@pytest.mark.parametrize("text,geo,kf,ri", LAYOUT_CASES)
+def test_device_positions_bit_exact(gpu, text, geo, kf, ri):
+    import torch
+
+    lay = _library_layout(text, geo, kf, REF_SETS[ri])
+    _, want = O.packed_layout(text, O.latent_geometry(*geo), kf, REF_SETS[ri])
+    got = lay.positions(0)
+    torch.cuda.synchronize()
+    assert np.array_equal(got.cpu().numpy(), want.astype(np.float32))
+
+
+@pytest.mark.parametrize("text,geo,kf,ri", LAYOUT_CASES[:4])
+def test_device_table_matches_checker(gpu, text, geo, kf, ri):
+    import torch
+
+    from h3attention import Runtime
+
+    lay = _library_layout(text, geo, kf, REF_SETS[ri])
+    _, pos = O.packed_layout(text, O.latent_geometry(*geo), kf, REF_SETS[ri])
+    inv = _inv_freq()
+    ref = O.rope_table_shared(pos.astype(np.float32), inv)
+    tab = lay.rope_table(torch.from_numpy(inv), 0)
+    # the two-step route (positions, then the shared-inv_freq table) agrees exactly
+    tab2 = Runtime.get(0).rope_table_shared(lay.positions(0), torch.from_numpy(inv).to(gpu))
+    torch.cuda.synchronize()
+    a = tab.cpu().view(torch.int16).numpy().view(np.uint16)
+    assert np.array_equal(a, tab2.cpu().view(torch.int16).numpy().view(np.uint16))
+    diff = np.abs(a.astype(np.int32) - ref.astype(np.int32))
+    assert diff.max() <= 1 and np.count_nonzero(diff) <= max(4, diff.size // 100000)
+
+
+def test_production_shape_fused(gpu):
+    """S = 15,731 (480x864, 5 s, 332 text tokens), H = 56, eps 1e-5
+    (H3Config.swift:32), rot 96 from the layout's table, all blocks kept:
+    the call the reference makes per block at this shape.  Checked on a
+    sample of query blocks across text, audio and video rows and two heads."""
+    import torch
+
+    from h3attention import BlockList, Runtime
+
+    lay = _library_layout(332, (864, 480, 120), [], [])
+    S, H = lay.total_tokens, 56
+    assert S == 15731
+    q, k, v = (O.fill_normal_bf16((S, H, 128), 31, st) for st in (1, 2, 3))
+    wq, wk = (O.fill_normal_bf16((128,), 31, st, 1.0, 0.02) for st in (4, 5))
+    inv = _inv_freq()
+    _, pos = O.packed_layout(332, O.latent_geometry(864, 480, 120))
+    tab = O.rope_table_shared(pos.astype(np.float32), inv)
+    bl = BlockList.dense(S)
+    rp, ci = bl.row_ptr, bl.col_idx
+    qbs, heads = [0, 2, 5, 60, 122], [0, 55]
+    qn, kn = O.prologue(q, wq, 1e-5, tab), O.prologue(k, wk, 1e-5, tab)
+    want = sum(O.attend_streaming(qn, kn, v, rp, ci, qblocks=qbs, heads=(h, h + 1)) for h in heads)
+
+    def dev(a):
+        return torch.from_numpy(a.view(np.int16)).view(torch.bfloat16).to(gpu)
+
+    qd, kd, vd = dev(q), dev(k), dev(v)
+    out = torch.empty_like(qd)
+    tab_d = lay.rope_table(torch.from_numpy(inv), 0)
+    Runtime.get(0).attn_fwd(q=qd, k=kd, v=vd, out=out, layout="SHD", scale=1 / np.sqrt(128), blocks=bl.on(0),
+                            q_norm=dev(wq), k_norm=dev(wk), eps=1e-5, rope_table=tab_d)
+    torch.cuda.synchronize()
+    got = O.bf16_to_f32(out.cpu().view(torch.int16).numpy().view(np.uint16)).transpose(1, 0, 2)
+    rows = np.concatenate([np.arange(b * 128, min(S, b * 128 + 128)) for b in qbs])
+    for h in heads:
+        err = np.abs(got[h, rows] - want[h, rows])
+        assert np.isfinite(got[h, rows]).all()
+        assert err.max() <= 2e-2 and err.mean() <= 2e-3, (h, err.max(), err.mean())

@@ -74,14 +74,14 @@ def test_rope_table_matches_checker(gpu):
     assert diff.max() <= 1 and np.count_nonzero(diff) <= 4
 
 
-@pytest.mark.parametrize("S,H,half", [(4096, 8, 64), (1000, 3, 48), (257, 2, 0)])
+@pytest.mark.parametrize("S,H,half", [(4096, 8, 64), (1000, 3, 48), (777, 2, 46), (257, 2, 0)])
 def test_prologue_matches_checker(gpu, S, H, half):
     import torch
 
     x = O.fill_normal_bf16((S, H, 128), 21, 1)
     w = O.fill_normal_bf16((128,), 21, 4, 1.0, 0.02)
     if half:
-        dims = (32, 48, 48) if half == 64 else (32, 32, 32)
+        dims = {64: (32, 48, 48), 48: (32, 32, 32), 46: (30, 32, 30)}[half]
         pos = np.stack([np.arange(S) % 17, np.arange(S) % 13, np.arange(S) % 11], 1).astype(np.int32)
         tab = O.rope_table(pos, dims=dims)
     else:
