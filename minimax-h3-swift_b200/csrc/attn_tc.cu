@@ -30,6 +30,7 @@
 #include <cuda.h>
 
 #include <climits>
+#include <type_traits>
 #include <cstdlib>
 
 #include "common.cuh"
@@ -52,7 +53,12 @@ struct __align__(8) Barriers {
   uint64_t o_full[2];
   uint32_t tmem_base;
   int32_t abort;
+  // union entry e: bit 0 tile 0 active, bit 1 tile 1 active, bit 2 last
+  // entry; written by the producer before the arrival that completes
+  // kv_full of K(e), read by the MMA issuer after waiting on it
+  int32_t info[16];
 };
+static_assert(sizeof(Barriers) <= 256, "barrier block");
 
 constexpr int kSmemTiles = 2 * kTileBytes + kStages * kTileBytes;
 constexpr int kSmemBytes = kSmemTiles + 1024 /*align slack*/ + 256 /*barriers*/;
@@ -290,11 +296,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = bars->tmem_base;
   // Register split: the launch gives 384 x 168; the producer/MMA warpgroup
-  // keeps 56 and the two softmax warpgroups take 224 each
-  // (4*32*56 + 8*32*224 = 64512 = 384*168; the host checks the launch count).
+  // keeps 72 and the two softmax warpgroups take 216 each
+  // (4*32*72 + 8*32*216 = 64512 = 384*168; the host checks the launch count).
+  // Neither side spills at this split.
 
   if (warp < 4) {
-    asm volatile("setmaxnreg.dec.sync.aligned.u32 56;");
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 72;");
    if (nkv > 0) {
     if (warp == 0) {
       // ------------------------------------------------------- TMA producer
@@ -310,7 +317,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         int n = 0;
         bool ok = true;
-        auto load = [&](const CUtensorMap* map, int jb) {
+        auto load = [&](const CUtensorMap* map, int jb, int info) {
           const int slot = n % kStages;
           const uint32_t ph = (uint32_t)((n / kStages) & 1);
           if (n == a.drop_item) {  // host-side fault injection for tests: this load never happens
@@ -322,6 +329,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             return;
           }
           uint32_t bar = smem_u32(&bars->kv_full[slot]);
+          if (info >= 0) bars->info[(n >> 1) & 15] = info;
           mbar_expect_tx(bar, kTileBytes);
           uint32_t dst = smem_u32(sKV + slot * kTileBytes);
           tma_load_3d(dst, map, bar, 0, jb * 128, h);
@@ -333,10 +341,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int c0 = i0 < tn[0] ? a.col_idx[tp0[0] + i0] : INT_MAX;
           const int c1 = i1 < tn[1] ? a.col_idx[tp0[1] + i1] : INT_MAX;
           const int u = min(c0, c1);
-          load(&tm_k, u);
-          if (ok) load(&tm_v, u);
           i0 += (c0 == u);
           i1 += (c1 == u);
+          const bool last = i0 >= tn[0] && i1 >= tn[1];
+          load(&tm_k, u, (c0 == u ? 1 : 0) | (c1 == u ? 2 : 0) | (last ? 4 : 0));
+          if (ok) load(&tm_v, u, -1);
         }
         // Drain: wait for the last loads to land before anyone may exit.
         if (!ok) {
@@ -353,92 +362,120 @@ __global__ void __launch_bounds__(kThreads, 1)
       // Union entry e owns ring items 2e (K) and 2e+1 (V).  Per entry, for
       // each tile in turn: the PV of the tile's previous entry (its P is ready
       // once the softmax arrives), then the tile's S for this entry, so the
-      // tiles ping-pong between MMA and softmax.  K(e) is released once the
-      // S of every tile active at e is issued; V(e) once both tiles' PVs of e
-      // are issued (at the latest while entry e+1 is processed).
+      // tiles ping-pong between MMA and softmax and their exponentials (the
+      // MUFU unit's load equals the tensor pipe's) rarely overlap.  K(e) is
+      // released once the S of every tile active at e is issued; V(e) once
+      // both tiles' PVs of e are issued (while entry e+1 is processed).
       if (lane == 0) {
         constexpr uint32_t kIdS = idesc_bf16(false);
         constexpr uint32_t kIdPV = idesc_bf16(true);
         bool ok = true;
-        for (int t = 0; t < ntile && ok; ++t) ok = mbar_wait(smem_u32(&bars->q_full[t]), 0, abort_flag, a.status, a.wait_limit_ns);
+        for (int t = 0; t < ntile && ok; ++t)
+          ok = mbar_wait(smem_u32(&bars->q_full[t]), 0, abort_flag, a.status, a.wait_limit_ns);
         tc_fence_after();
-        int pend[2] = {-1, -1};  // union entry whose PV is still due, per tile
-        int ns[2] = {0, 0};      // S issued per tile
+        // Per-tile state lives in named scalars and every per-tile step is
+        // instantiated for a compile-time tile index, so nothing here is
+        // dynamically indexed (which would put it in local memory, on the
+        // issue path).
+        int pend0 = -1, pend1 = -1;  // union entry whose PV is still due, per tile
+        int ns0 = 0, ns1 = 0;        // S issued per tile
+        int v_ready = -1;            // union entry whose V tile is known to have landed
         auto ring_wait = [&](int item) -> bool {
           const int slot = item % kStages;
-          if (!mbar_wait(smem_u32(&bars->kv_full[slot]), (uint32_t)((item / kStages) & 1), abort_flag, a.status, a.wait_limit_ns))
+          if (!mbar_wait(smem_u32(&bars->kv_full[slot]), (uint32_t)((item / kStages) & 1), abort_flag, a.status,
+                         a.wait_limit_ns))
             return false;
           tc_fence_after();
           return true;
         };
-        auto issue_pv = [&](int t) -> bool {
-          const int e = pend[t];
-          if (!mbar_wait(smem_u32(&bars->p_full[t]), (uint32_t)((ns[t] - 1) & 1), abort_flag, a.status, a.wait_limit_ns)) return false;
+        auto issue_pv = [&](auto tile) -> bool {
+          constexpr int t = decltype(tile)::value;
+          int& pend = t == 0 ? pend0 : pend1;
+          const int nst = t == 0 ? ns0 : ns1;
+          const int other = t == 0 ? pend1 : pend0;
+          const int e = pend;
+          if (!mbar_wait(smem_u32(&bars->p_full[t]), (uint32_t)((nst - 1) & 1), abort_flag, a.status,
+                         a.wait_limit_ns))
+            return false;
           tc_fence_after();
           const int item = 2 * e + 1;
-          if (!ring_wait(item)) return false;
+          if (v_ready != e) {
+            if (!ring_wait(item)) return false;
+            v_ready = e;
+          }
           const uint32_t vbase = smem_u32(sKV + (item % kStages) * kTileBytes);
 #pragma unroll
           for (int kk = 0; kk < 8; ++kk)
             mma_ts(tmem + 256 * t + 128, tmem + 256 * t + kk * 8, smem_desc(vbase + kk * 2048, kHalfBytes, 1024),
-                   kIdPV, (ns[t] > 1 || kk > 0) ? 1u : 0u);
-          pend[t] = -1;
-          if (pend[t ^ 1] != e) tc_commit(smem_u32(&bars->kv_empty[item % kStages]));
+                   kIdPV, (nst > 1 || kk > 0) ? 1u : 0u);
+          pend = -1;
+          if (other != e) tc_commit(smem_u32(&bars->kv_empty[item % kStages]));
           return true;
         };
-        int i0 = 0, i1 = 0, e = 0;
-        while (ok && (i0 < tn[0] || i1 < tn[1])) {
-          const int c0 = i0 < tn[0] ? a.col_idx[tp0[0] + i0] : INT_MAX;
-          const int c1 = i1 < tn[1] ? a.col_idx[tp0[1] + i1] : INT_MAX;
-          const int u = min(c0, c1);
-          const bool act[2] = {c0 == u, c1 == u};
-          bool kwaited = false;
-          for (int t = 0; t < 2 && ok; ++t) {
-            if (pend[t] >= 0) ok = issue_pv(t);
-            if (ok && act[t]) {
-              if (!kwaited) {
-                ok = ring_wait(2 * e);
-                kwaited = true;
-                if (!ok) break;
-              }
-              const uint32_t qa = smem_u32(sQ + t * kTileBytes);
-              const uint32_t kbase = smem_u32(sKV + ((2 * e) % kStages) * kTileBytes);
+        auto issue_s = [&](auto tile, int e) {
+          constexpr int t = decltype(tile)::value;
+          const uint32_t qa = smem_u32(sQ + t * kTileBytes);
+          const uint32_t kbase = smem_u32(sKV + ((2 * e) % kStages) * kTileBytes);
 #pragma unroll
-              for (int kk = 0; kk < 8; ++kk) {
-                const uint32_t off = (kk >> 2) * kHalfBytes + (kk & 3) * 32;
-                mma_ss(tmem + 256 * t, smem_desc(qa + off, 16, 1024), smem_desc(kbase + off, 16, 1024), kIdS,
-                       kk > 0 ? 1u : 0u);
-              }
-              tc_commit(smem_u32(&bars->s_full[t]));
-              pend[t] = e;
-              ++ns[t];
-            }
+          for (int kk = 0; kk < 8; ++kk) {
+            const uint32_t off = (kk >> 2) * kHalfBytes + (kk & 3) * 32;
+            mma_ss(tmem + 256 * t, smem_desc(qa + off, 16, 1024), smem_desc(kbase + off, 16, 1024), kIdS,
+                   kk > 0 ? 1u : 0u);
           }
+          tc_commit(smem_u32(&bars->s_full[t]));
+          (t == 0 ? pend0 : pend1) = e;
+          ++(t == 0 ? ns0 : ns1);
+        };
+        using T0 = std::integral_constant<int, 0>;
+        using T1 = std::integral_constant<int, 1>;
+        // The producer hands over each union entry's active tiles in shared
+        // memory, so this thread issues no global loads.
+        for (int e = 0; ok; ++e) {
+          if (pend0 >= 0) ok = issue_pv(T0{});
+          if (!ok || !ring_wait(2 * e)) {
+            ok = false;
+            break;
+          }
+          const int info = ((volatile int32_t*)bars->info)[e & 15];
+          if (info & 1) issue_s(T0{}, e);
+          if (pend1 >= 0) ok = issue_pv(T1{});
+          if (ok && (info & 2)) issue_s(T1{}, e);
           if (ok) tc_commit(smem_u32(&bars->kv_empty[(2 * e) % kStages]));
-          i0 += act[0];
-          i1 += act[1];
-          ++e;
+          if (info & 4) break;
         }
-        for (int t = 0; t < ntile && ok; ++t) {
-          if (pend[t] >= 0) ok = issue_pv(t);
-          if (ok) tc_commit(smem_u32(&bars->o_full[t]));
+        if (ok && ntile > 0) {
+          if (pend0 >= 0) ok = issue_pv(T0{});
+          if (ok) tc_commit(smem_u32(&bars->o_full[0]));
         }
-        if (!ok) {  // let every issued MMA retire before TMEM is released
-          tc_commit(smem_u32(&bars->o_full[0]));
+        if (ok && ntile > 1) {
+          if (pend1 >= 0) ok = issue_pv(T1{});
+          if (ok) tc_commit(smem_u32(&bars->o_full[1]));
         }
+        // on an abort: every MMA issued so far retires before the exit
+        // releases TMEM
+        if (!ok)
+          for (int t = 0; t < ntile; ++t) tc_commit(smem_u32(&bars->o_full[t]));
       }
     }
    }
   } else {
-    asm volatile("setmaxnreg.inc.sync.aligned.u32 224;");
-   if (nkv > 0) {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 216;");
     {
       // --------------------------------------------------- softmax + epilogue
       const int t = (warp - 4) >> 2;
       const int q = warp & 3;  // TMEM lane quarter this warp may access
-      if (t < ntile && tn[t] > 0) {
-        const int p0 = tp0[t];
-        const int nkv = tn[t];
+      const int p0 = t ? tp0[1] : tp0[0];
+      const int nkv = t ? tn[1] : tn[0];
+      if (t < ntile && nkv == 0) {
+        // a query block with no kept key block: O / max(l, 1e-30) with l = 0
+        const int row = (qb0 + t) * 128 + 32 * q + lane;
+        if (row < a.seq_len) {
+          uint4* go = reinterpret_cast<uint4*>(a.o + (int64_t)h * a.o_head + (int64_t)row * a.o_tok);
+#pragma unroll
+          for (int c = 0; c < 16; ++c) go[c] = make_uint4(0, 0, 0, 0);
+        }
+      }
+      if (t < ntile && nkv > 0) {
         const uint32_t lane_base = (uint32_t)(32 * q) << 16;
         const uint32_t tS = tmem + lane_base + 256 * t;
         const uint32_t tO = tS + 128;
@@ -550,17 +587,18 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
-   }
   }
 
   // ------------------------------------------------------------------ exit
   tc_fence_before();
   __syncthreads();
   if (bars->abort) {
-    // an aborted MMA warp committed to o_full[0]; wait (bounded) for it so
-    // that no MMA is still writing TMEM when it is released
+    // every issuer committed its MMAs to o_full[t], aborted or not; wait
+    // (bounded) for them so that no MMA is still writing TMEM when it is
+    // released
     volatile int32_t zero = 0;
-    if (warp == 2) mbar_wait(smem_u32(&bars->o_full[0]), 0, &zero, nullptr);
+    if (warp == 2)
+      for (int t = 0; t < ntile; ++t) mbar_wait(smem_u32(&bars->o_full[t]), 0, &zero, nullptr);
     __syncwarp();
   }
   if (warp == 2) {
@@ -614,7 +652,7 @@ template <int EMU>
 cudaError_t launch_variant(dim3 grid, cudaStream_t s, const CUtensorMap& mq, const CUtensorMap& mk,
                            const CUtensorMap& mv, const AttnLaunch& a) {
   // function attributes are per device context: remember them per device
-  static bool attr_set[64] = {};
+  static bool attr_set[64] = {};  // one table per template instance
   int dev = 0;
   cudaError_t de = cudaGetDevice(&dev);
   if (de != cudaSuccess) return de;
@@ -655,10 +693,7 @@ cudaError_t launch_attn_tc(const AttnLaunch& a, cudaStream_t s, std::string* err
   switch (emu) {
     case 0: return launch_variant<0>(grid, s, mq, mk, mv, a);
     case 2: return launch_variant<2>(grid, s, mq, mk, mv, a);
-    case 3: return launch_variant<3>(grid, s, mq, mk, mv, a);
     case 4: return launch_variant<4>(grid, s, mq, mk, mv, a);
-    case 5: return launch_variant<5>(grid, s, mq, mk, mv, a);
-    case 6: return launch_variant<6>(grid, s, mq, mk, mv, a);
     default: return launch_variant<kDefaultEmu>(grid, s, mq, mk, mv, a);
   }
 }

@@ -30,3 +30,23 @@ def gpu():
     import torch
 
     return torch.device("cuda:0")
+
+
+@pytest.fixture(autouse=True)
+def _device_status_clean(request):
+    """After every GPU test: the kernels' device status word must be clean
+    (a bounded wait that gave up records H3C_ERR_TIMEOUT there; the calls
+    themselves are asynchronous and cannot report it)."""
+    yield
+    if request.node.get_closest_marker("gpu") is None or "no_status_check" in request.keywords:
+        return
+    if not has_gpu():
+        return
+    import torch
+
+    from h3attention import Runtime
+
+    for d in range(torch.cuda.device_count()):
+        if d in Runtime._by_device:
+            torch.cuda.synchronize(d)
+            Runtime._by_device[d].device_status()

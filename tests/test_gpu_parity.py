@@ -152,6 +152,36 @@ def test_attention_matches_checker(gpu, kernel, name):
 
 
 @pytest.mark.parametrize("kernel", ["mma_sync", "tcgen05"])
+def test_empty_rows_give_zeros(gpu, kernel):
+    """A caller-supplied block list may leave query blocks without any kept
+    key block; their rows come out as zeros (O / max(l, 1e-30) with l = 0),
+    as in the checker.  Row 1 empties one tile of a two-tile CTA, rows 4-5
+    a whole CTA, and the last row a single-tile CTA."""
+    import torch
+
+    from h3attention import _lib
+
+    S, H = 1100, 2
+    q, k, v, rp, ci = _case(S, H, dict(seq_len=S, frames=11, height=10, width=10, n_random=1, seed=6))
+    rows = [ci[rp[i]:rp[i + 1]] for i in range(len(rp) - 1)]
+    for i in (1, 4, 5, len(rows) - 1):
+        rows[i] = rows[i][:0]
+    rp = np.concatenate([[0], np.cumsum([len(r) for r in rows])]).astype(np.int32)
+    ci = np.concatenate(rows).astype(np.int32)
+    want = O.attend_streaming(q, k, v, rp, ci)
+    qd, kd, vd = (_t(a, gpu) for a in (q, k, v))
+    out = torch.full_like(qd, float("nan"))
+    blocks = (torch.from_numpy(rp).to(gpu), torch.from_numpy(ci).to(gpu))
+    flags = _lib.H3C_KERNEL_MMA_SYNC if kernel == "mma_sync" else 0
+    _rt().attn_fwd(q=qd, k=kd, v=vd, out=out, layout="SHD", scale=1 / np.sqrt(128), blocks=blocks, flags=flags)
+    torch.cuda.synchronize()
+    got = _np(out)
+    for i in (1, 4, 5, len(rows) - 1):
+        assert np.all(got[i * 128:min(S, i * 128 + 128)] == 0), i
+    _check_attn(got, want)
+
+
+@pytest.mark.parametrize("kernel", ["mma_sync", "tcgen05"])
 def test_fused_prologue_matches_checker(gpu, kernel):
     import torch
 
