@@ -30,6 +30,8 @@ package final class CUDABackend: H3AttentionBackend, @unchecked Sendable {
     private var rowPtr: UnsafeMutableRawPointer?
     private var colIdx: UnsafeMutableRawPointer?
     private var seqLen = 0
+    private var ropeTable: UnsafeMutableRawPointer?   // bf16 [S, 3n, 4], built once per render
+    private var ropeHalf: Int32 = 0
 
     package required init() {
         var c: OpaquePointer?
@@ -39,6 +41,7 @@ package final class CUDABackend: H3AttentionBackend, @unchecked Sendable {
     deinit {
         if let rowPtr { cudaFreeBridge(rowPtr) }
         if let colIdx { cudaFreeBridge(colIdx) }
+        if let ropeTable { cudaFreeBridge(ropeTable) }
         if let ctx { h3c_destroy(ctx) }
     }
 
@@ -58,6 +61,24 @@ package final class CUDABackend: H3AttentionBackend, @unchecked Sendable {
             throw H3Error.unavailableFeature(feature: "b200 block list", detail: "device build failed")
         }
         seqLen = Int(spec.seq_len)
+    }
+
+    /// The render's RoPE table from its packed layout and the checkpoint's
+    /// shared `rope.inv_freq` (device fp32, `n` entries): what
+    /// `prepareRender` builds in H3Transformer.swift:263-276, for the fused
+    /// prologue (H3C_FUSE_PROLOGUE with `a.rope_table` / `a.rope_half`).
+    package func prepareRope(layout: h3c_layout_spec, invFreq: UnsafePointer<Float>, n: Int32) throws {
+        var spec = layout
+        var nseg: Int32 = 0
+        var total: Int64 = 0
+        guard h3c_packed_layout(&spec, nil, 0, &nseg, &total) == H3C_OK else {
+            throw H3Error.unavailableFeature(feature: "b200 rope table", detail: "layout refused")
+        }
+        ropeTable = cudaMallocBridge(Int(total) * Int(3 * n) * 8)
+        guard let ctx, h3c_rope_table_layout(ctx, &spec, invFreq, n, ropeTable, total, nil) == H3C_OK else {
+            throw H3Error.unavailableFeature(feature: "b200 rope table", detail: "device build failed")
+        }
+        ropeHalf = 3 * n
     }
 
     package func attend(queries: MLXArray, keys: MLXArray, values: MLXArray,
