@@ -316,10 +316,14 @@ def test_backend_seam_fused_and_decline(gpu):
     assert np.abs(got - want).max() <= 2e-2
 
 
-def test_qkv_direct_views(gpu):
-    """q, k, v read straight from one [S, 3*H*D] QKV GEMM output (Q|K|V
-    blocked, head-major inside, DiTBlock.swift:338-344) through strided
-    views, with the fused prologue: equals the call on split copies."""
+@pytest.mark.parametrize("vendor", ["blocked", "interleaved"])
+def test_qkv_direct_views(gpu, vendor):
+    """q, k, v read straight from one [S, 3*H*D] QKV GEMM output through
+    strided views, with the fused prologue: equals the call on split copies.
+    Both checkpoint layouts of attn.qkv_proj (FRAGILE_CONTRACTS.md section 9)
+    are views: Comfy-Org's blocked (3, heads, headDim) Q|K|V
+    (DiTBlock.swift:338-344) and DeepBeepMeep's per-head interleaved
+    (heads, 3, headDim), so neither needs the permute-on-load."""
     import torch
 
     from h3attention import BlockList, MaskSpec
@@ -331,8 +335,13 @@ def test_qkv_direct_views(gpu):
     pos = np.stack([np.arange(S) // 300, (np.arange(S) // 20) % 15, np.arange(S) % 20], 1).astype(np.int32)
     tab = _t(O.rope_table(pos), gpu)
     bl = BlockList.build(MaskSpec(seq_len=S, frames=5, height=15, width=20, n_random=1, seed=2))
-    views = [qkv[:, i * H * 128:(i + 1) * H * 128].view(S, H, 128) for i in range(3)]  # strided, no copy
-    assert views[0].stride() == (3 * H * 128, 128, 1)
+    if vendor == "blocked":
+        views = [qkv[:, i * H * 128:(i + 1) * H * 128].view(S, H, 128) for i in range(3)]  # strided, no copy
+        assert views[0].stride() == (3 * H * 128, 128, 1)
+    else:
+        per_head = qkv.view(S, H, 3, 128)
+        views = [per_head[:, :, i] for i in range(3)]
+        assert views[0].stride() == (3 * H * 128, 3 * 128, 1)
     out_v = torch.empty((S, H, 128), dtype=torch.bfloat16, device=gpu)
     _rt().attn_fwd(q=views[0], k=views[1], v=views[2], out=out_v, layout="SHD", scale=128 ** -0.5,
                    blocks=bl.on(gpu), q_norm=wq, k_norm=wk, eps=1e-6, rope_table=tab)
