@@ -195,6 +195,7 @@ class CUDABackend(_KernelBackend):
         self.blocks: Optional[BlockList] = None
         self.min_sequence_length = 0
         self.dense_blocks: Sequence[int] = ()
+        self.rope = None
 
     @classmethod
     def is_available(cls, machine: Machine) -> bool:
@@ -213,6 +214,14 @@ class CUDABackend(_KernelBackend):
         self.min_sequence_length = min_sequence_length
         self.dense_blocks = tuple(dense_blocks)
         return self.blocks
+
+    def render_rope_table(self, layout, inv_freq, device: int = 0):
+        """The render's RoPE table from its packed layout and the
+        checkpoint's shared ``rope.inv_freq`` (``prepareRender``,
+        H3Transformer.swift:263-276), built on the device once per render;
+        pass it as ``rope_table`` to ``attend_fused``."""
+        self.rope = layout.rope_table(inv_freq, device)
+        return self.rope
 
     def attend(self, queries, keys, values, scale, mask, context):
         if self.spec is None or mask is not None:

@@ -54,6 +54,19 @@ class MaskSpec:
         return s
 
     @staticmethod
+    def for_layout(layout, **params) -> "MaskSpec":
+        """The mask of a render's packed sequence (``layout.PackedLayout``):
+        every row before the target video (text, conditions, references,
+        audio) is prefix, the video is the latent_t x (latent_h/patch) x
+        (latent_w/patch) token lattice.  ``params``: radius_*, n_random,
+        seed, cell_*."""
+        g = layout.geometry
+        v0, v1 = layout.range_of("video")
+        assert v1 == layout.total_tokens, "the target video is the last segment"
+        return MaskSpec(seq_len=layout.total_tokens, frames=g.latent_t, height=g.latent_h // g.patch,
+                        width=g.latent_w // g.patch, prefix_len=v0, **params)
+
+    @staticmethod
     def dense(seq_len: int) -> "MaskSpec":
         """Every block kept: the whole sequence is prefix."""
         return MaskSpec(seq_len=seq_len, frames=0, height=0, width=0, prefix_len=seq_len)

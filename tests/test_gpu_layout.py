@@ -88,3 +88,46 @@ def test_production_shape_fused(gpu):
         err = np.abs(got[h, rows] - want[h, rows])
         assert np.isfinite(got[h, rows]).all()
         assert err.max() <= 2e-2 and err.mean() <= 2e-3, (h, err.max(), err.mean())
+
+
+def test_render_through_the_seam(gpu):
+    """A render end to end through the seam mirror: the packed layout (text,
+    one keyframe, audio, video) gives the mask geometry and the device RoPE
+    table; CUDABackend.attend_fused runs the fused call on [H, S, D]
+    pre-norm q/k.  Checked against the checker on sampled query blocks
+    (prefix rows, the keyframe's rows, video rows)."""
+    import torch
+
+    from h3attention import AttentionContext, CUDABackend, MaskSpec
+
+    lay = _library_layout(332, (864, 480, 120), [0], [])
+    S, H = lay.total_tokens, 4
+    be = CUDABackend()
+    spec = MaskSpec.for_layout(lay, radius_h=2, radius_w=2, n_random=4, seed=11)
+    bl = be.prepare_render(spec)
+    inv = _inv_freq()
+    table = be.render_rope_table(lay, torch.from_numpy(inv), 0)
+    q, k, v = (O.fill_normal_bf16((S, H, 128), 41, st) for st in (1, 2, 3))
+    wq, wk = (O.fill_normal_bf16((128,), 41, st, 1.0, 0.02) for st in (4, 5))
+    _, pos = O.packed_layout(332, O.latent_geometry(864, 480, 120), [0])
+    tab = O.rope_table_shared(pos.astype(np.float32), inv)
+    qbs = [0, 3, 6, 40, bl.n_blocks - 1]
+    want = O.attend_streaming(O.prologue(q, wq, 1e-5, tab), O.prologue(k, wk, 1e-5, tab), v, bl.row_ptr,
+                              bl.col_idx, qblocks=qbs)
+
+    def hsd(a):
+        return torch.from_numpy(np.ascontiguousarray(a.transpose(1, 0, 2)).view(np.int16)).view(torch.bfloat16).to(gpu)
+
+    def dev(a):
+        return torch.from_numpy(a.view(np.int16)).view(torch.bfloat16).to(gpu)
+
+    ctx = AttentionContext(block_index=3, block_count=50, schedule_progress=0.5, sequence_length=S,
+                           video_span=(spec.prefix_len, S))
+    out = be.attend_fused(hsd(q), hsd(k), hsd(v), 128 ** -0.5, dev(wq), dev(wk), 1e-5, table, ctx)
+    assert out is not None
+    torch.cuda.synchronize()
+    got = O.bf16_to_f32(out.cpu().view(torch.int16).numpy().view(np.uint16))
+    rows = np.concatenate([np.arange(b * 128, min(S, b * 128 + 128)) for b in qbs])
+    err = np.abs(got[:, rows] - want[:, rows])
+    assert np.isfinite(got[:, rows]).all()
+    assert err.max() <= 2e-2 and err.mean() <= 2e-3, (err.max(), err.mean())

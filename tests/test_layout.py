@@ -169,3 +169,22 @@ def test_production_shape():
     c, s = O.bf16_to_f32(tab[..., 0]), O.bf16_to_f32(tab[..., 2])
     assert np.all(O.bf16_to_f32(tab[..., 3]) == c) and np.all(O.bf16_to_f32(tab[..., 1]) == -s)
     assert np.abs(c * c + s * s - 1).max() < 1e-2
+
+
+def test_mask_spec_for_layout():
+    """The mask geometry of a render follows from its packed layout: every
+    row before the target video is prefix, the video is the token lattice."""
+    from h3attention import BlockList, MaskSpec
+
+    lay = _library_layout(332, (864, 480, 120), [0], [])
+    spec = MaskSpec.for_layout(lay, radius_h=2, radius_w=2, n_random=4, seed=7)
+    assert (spec.seq_len, spec.prefix_len) == (lay.total_tokens, lay.range_of("video")[0])
+    assert (spec.frames, spec.height, spec.width) == (37, 15, 27)
+    assert spec.prefix_len + spec.frames * spec.height * spec.width == spec.seq_len
+    bl = BlockList.build(spec)
+    rp, ci = O.blockmask_build(O.mask_spec(**{k: getattr(spec, k) for k in (
+        "seq_len", "frames", "height", "width", "prefix_len", "radius_h", "radius_w", "n_random", "seed")}))
+    assert np.array_equal(bl.row_ptr, rp) and np.array_equal(bl.col_idx, ci)
+    npb = -(-spec.prefix_len // 128)
+    for i in range(npb):  # prefix rows are dense
+        assert bl.row_ptr[i + 1] - bl.row_ptr[i] == bl.n_blocks
