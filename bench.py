@@ -247,7 +247,7 @@ def run_ours(args):
     if mode == "heads":
         h0, h1 = head_range(rank, ws, H)
         rows, hl = S, h1 - h0
-    elif mode == "seq":
+    elif mode in ("seq", "seq_torch"):
         rows, hl = seq_shard_len(S, ws), H
     else:
         rows, hl = S, H
@@ -259,8 +259,23 @@ def run_ours(args):
     blocks = bl.on(dev)
     scale = 128 ** -0.5
     if mode == "seq":
-        # every rank: all-to-all, the fused call on H/P heads of the whole
-        # sequence, all-to-all back; the work of one call is shared
+        # every rank: its token shard of all heads in, the library's
+        # sequence-sharded call (NCCL all-to-alls over head chunks, pipelined
+        # with the fused call on the chunks), its shard of the output back
+        uid = [Runtime.comm_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        rt.comm_init(uid[0], ws, rank)
+        job_flops = bl.flops(H)
+        out = torch.empty_like(q)
+
+        def step():
+            rt.attn_fwd_seqshard(q=q, k=k, v=v, out=out, layout="SHD", scale=scale, blocks=blocks, q_norm=wq,
+                                 k_norm=wk, eps=EPS, rope_table=tab, seq_len=S)
+
+        fused = None
+        scaling = "strong"
+    elif mode == "seq_torch":
+        # the same layout over torch.distributed all_to_all_single, unpipelined
         attend = cuda_attend_fn(rt, blocks, S, scale, q_norm=wq, k_norm=wk, eps=EPS, rope_table=tab)
         job_flops = bl.flops(H)
         out = torch.empty_like(q)
@@ -278,7 +293,8 @@ def run_ours(args):
 
         def step():
             rt.attn_fwd_args(fused)
-    flops = bl.flops(hl if mode != "seq" else H // ws)  # this rank's attention work per call
+    seqm = mode in ("seq", "seq_torch")
+    flops = bl.flops(hl if not seqm else H // ws)  # this rank's attention work per call
 
     for _ in range(args.warmup):
         step()
@@ -298,7 +314,7 @@ def run_ours(args):
 
     # Roofline pass: the attention kernel alone on pre-normalised Q/K, each
     # launch bracketed by events on the launching stream.
-    if mode == "seq":  # the per-rank kernel runs on [S, H/P] after the exchange
+    if seqm:  # the per-rank kernel runs on [S, H/P] after the exchange
         rq, rk, rv = (torch.empty((S, H // ws, 128), dtype=bf, device=dev) for _ in range(3))
         for t_, st_ in ((rq, STREAM_Q), (rk, STREAM_K), (rv, STREAM_V)):
             rt.fill_normal(t_, wl.seed + rank, st_)
@@ -325,7 +341,7 @@ def run_ours(args):
     # End to end through the public host-buffer call (h3attention.host):
     # pinned host [H, S, D] q/k/v in, fused call, pinned host output back,
     # every step; uploads, compute and downloads of head chunks overlap.
-    if mode == "seq":
+    if seqm:
         hq, hk, hv = (t.cpu().pin_memory() for t in (q, k, v))
         hout = torch.empty(out.shape, dtype=bf).pin_memory()
 
@@ -369,7 +385,9 @@ def run_ours(args):
                        "density": round(bl.density, 4), "kept_blocks": bl.nnz, "flops_per_call": flops,
                        "l2": "inputs larger than L2 (no flush)",
                        "parallelism": {"replica": f"replicas x{ws} (weak)", "heads": f"head-sharded x{ws}",
-                                       "seq": f"sequence-sharded x{ws} (NCCL all-to-all)"}[mode],
+                                       "seq": f"sequence-sharded x{ws} (NCCL all-to-alls pipelined over head "
+                                               "chunks, C ABI)",
+                                       "seq_torch": f"sequence-sharded x{ws} (torch all_to_all_single)"}[mode],
                        "prologue": (f"fused RMSNorm (eps {EPS:g}) + RoPE from the packed layout (rot 96, shared "
                                     "inv_freq)" if wl.render else
                                     f"fused RMSNorm (eps {EPS:g}) + RoPE (t/h/w 32/48/48, theta 1e4)")},
@@ -400,7 +418,7 @@ def main():
     ap.add_argument("--config", default="config2",
                     help="config1..config4, config5@<density> or production; default config2 (the 5 s 1344x768 clip)")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--mode", default="replica", choices=["replica", "heads", "seq"],
+    ap.add_argument("--mode", default="replica", choices=["replica", "heads", "seq", "seq_torch"],
                     help="N>1 layout: independent full calls per rank (weak), heads split across ranks, or "
                          "sequence-sharded with an all-to-all (strong)")
     ap.add_argument("--cpu-budget", type=float, default=15.0, help="seconds of CPU baseline sampling")

@@ -17,6 +17,8 @@
 #include <cstring>
 #include <mutex>
 
+#include <cstdlib>
+
 #include "common.cuh"
 
 namespace {
@@ -67,19 +69,23 @@ h3c_status fail(h3c_ctx* ctx, h3c_status st, const std::string& msg) {
   return st;
 }
 
-// [S_r, H, D] strided view <-> [P][S_r][H/P][D] contiguous, 16-byte vectors.
-// dir 0: view -> packed (before sending); dir 1: packed -> view (after receiving).
+// One head chunk of the exchange: heads [h0, h0 + hc) of every rank's group
+// of hp heads.  [S_r, H, D] strided view <-> [P][S_r][hc][D] contiguous,
+// 16-byte vectors.  dir 0: view -> packed (before sending); dir 1: packed ->
+// view (after receiving).
 __global__ void pack_kernel(uint16_t* __restrict__ view, int64_t tok, int64_t head, uint16_t* __restrict__ packed,
-                            int32_t s_r, int32_t heads, int32_t hp, int dir) {
-  const int64_t n = (int64_t)s_r * heads * 16;  // 16-byte chunks
+                            int32_t s_r, int32_t P, int32_t hp, int32_t h0, int32_t hc, int dir) {
+  const int64_t n = (int64_t)s_r * P * hc * 16;  // 16-byte chunks
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
     const int c = (int)(i & 15);
-    const int64_t rh = i >> 4;
-    const int h = (int)(rh % heads);
-    const int64_t s = rh / heads;
-    const int p = h / hp, hl = h - p * hp;
+    int64_t r = i >> 4;
+    const int hl = (int)(r % hc);
+    r /= hc;
+    const int64_t s = r % s_r;
+    const int p = (int)(r / s_r);
+    const int h = p * hp + h0 + hl;
     uint4* a = reinterpret_cast<uint4*>(view + s * tok + (int64_t)h * head) + c;
-    uint4* b = reinterpret_cast<uint4*>(packed + (((int64_t)p * s_r + s) * hp + hl) * 128) + c;
+    uint4* b = reinterpret_cast<uint4*>(packed + (((int64_t)p * s_r + s) * hc + hl) * 128) + c;
     if (dir == 0) *b = *a;
     else *a = *b;
   }
@@ -87,11 +93,18 @@ __global__ void pack_kernel(uint16_t* __restrict__ view, int64_t tok, int64_t he
 
 }  // namespace
 
+constexpr int kMaxChunks = 8;
+constexpr int kDefaultChunks = 1;
+
 struct h3c_comm_state {
   ncclComm_t_ comm = nullptr;
   int nranks = 0, rank = 0;
   void* buf = nullptr;
   size_t buf_bytes = 0;
+  // the exchange stream and the events that chain it with the caller's
+  // stream, created with the communicator
+  cudaStream_t side = nullptr;
+  cudaEvent_t start = nullptr, in_done[kMaxChunks] = {}, attn_done[kMaxChunks] = {}, out_done = nullptr;
 };
 
 namespace {
@@ -130,6 +143,17 @@ h3c_status h3c_comm_init(h3c_ctx* ctx, const h3c_comm_id* id, int nranks, int ra
   st->nranks = nranks;
   st->rank = rank;
   ctx->comm = st;
+  cudaError_t ce = cudaStreamCreateWithFlags(&st->side, cudaStreamNonBlocking);
+  if (ce == cudaSuccess) ce = cudaEventCreateWithFlags(&st->start, cudaEventDisableTiming);
+  if (ce == cudaSuccess) ce = cudaEventCreateWithFlags(&st->out_done, cudaEventDisableTiming);
+  for (int c = 0; c < kMaxChunks && ce == cudaSuccess; ++c) {
+    ce = cudaEventCreateWithFlags(&st->in_done[c], cudaEventDisableTiming);
+    if (ce == cudaSuccess) ce = cudaEventCreateWithFlags(&st->attn_done[c], cudaEventDisableTiming);
+  }
+  if (ce != cudaSuccess) {
+    h3c_comm_destroy(ctx);
+    return fail(ctx, H3C_ERR_CUDA, std::string("h3c_comm_init: stream/event creation: ") + cudaGetErrorString(ce));
+  }
   return H3C_OK;
 }
 
@@ -139,6 +163,16 @@ h3c_status h3c_comm_destroy(h3c_ctx* ctx) {
   if (!st) return H3C_OK;
   cudaSetDevice(ctx->device);
   if (st->buf) cudaFree(st->buf);
+  if (st->side) {
+    cudaStreamSynchronize(st->side);
+    cudaStreamDestroy(st->side);
+  }
+  for (cudaEvent_t e : {st->start, st->out_done})
+    if (e) cudaEventDestroy(e);
+  for (int c = 0; c < kMaxChunks; ++c) {
+    if (st->in_done[c]) cudaEventDestroy(st->in_done[c]);
+    if (st->attn_done[c]) cudaEventDestroy(st->attn_done[c]);
+  }
   Nccl* n = nccl();
   if (n && st->comm) n->CommDestroy(st->comm);
   delete st;
@@ -177,6 +211,7 @@ h3c_status h3c_attn_fwd_seqshard(h3c_ctx* ctx, const h3c_attn_args* args, void* 
   if (st->buf_bytes < need) {
     if (st->buf) {
       H3_CUDA_TRY(ctx, cudaStreamSynchronize(s));
+      H3_CUDA_TRY(ctx, cudaStreamSynchronize(st->side));
       cudaFree(st->buf);
       st->buf = nullptr;
       st->buf_bytes = 0;
@@ -184,21 +219,33 @@ h3c_status h3c_attn_fwd_seqshard(h3c_ctx* ctx, const h3c_attn_args* args, void* 
     H3_CUDA_TRY(ctx, cudaMalloc(&st->buf, need));
     st->buf_bytes = need;
   }
-  // layout: [send | q_x | k_x | v_x | o_x]; o_x is packed back through send
+  // layout: [send | q_x | k_x | v_x | o_x]; each is split into head chunks
+  // (chunk c holds heads [h0, h0 + hc) of every rank's group, all tokens);
+  // o_x comes back through the chunk's part of send.
   uint16_t* send = (uint16_t*)st->buf;
   uint16_t* qx = send + elems;
   uint16_t* kx = qx + elems;
   uint16_t* vx = kx + elems;
   uint16_t* ox = vx + elems;
-  const size_t chunk = (size_t)s_r * hp * 128;  // elements exchanged with one peer
   const int threads = 256;
   const int blocks = ctx->prop.multiProcessorCount * 8;
+  // Pipeline over head chunks: the exchange of chunk c+1 (side stream)
+  // overlaps the attention of chunk c (caller's stream), and the output of
+  // chunk c travels back while chunk c+1 computes.
+  static int chunks_env = -1;  // H3C_SEQ_CHUNKS: head chunks of the pipeline (tuning knob)
+  if (chunks_env < 0) {
+    const char* e = getenv("H3C_SEQ_CHUNKS");
+    chunks_env = e ? atoi(e) : kDefaultChunks;
+    if (chunks_env < 1 || chunks_env > kMaxChunks) chunks_env = kDefaultChunks;
+  }
+  const int nchunk = hp < chunks_env ? hp : chunks_env;
+  cudaStream_t x = st->side;
 
-  auto exchange = [&](uint16_t* src, uint16_t* dst) -> h3c_status {
+  auto exchange = [&](uint16_t* src, uint16_t* dst, size_t per_peer) -> h3c_status {
     if (n->GroupStart() != 0) return fail(ctx, H3C_ERR_NCCL, "ncclGroupStart");
     for (int p = 0; p < P; ++p) {
-      if (n->Send(src + p * chunk, chunk, kNcclBfloat16, p, st->comm, s) != 0 ||
-          n->Recv(dst + p * chunk, chunk, kNcclBfloat16, p, st->comm, s) != 0) {
+      if (n->Send(src + p * per_peer, per_peer, kNcclBfloat16, p, st->comm, x) != 0 ||
+          n->Recv(dst + p * per_peer, per_peer, kNcclBfloat16, p, st->comm, x) != 0) {
         n->GroupEnd();
         return fail(ctx, H3C_ERR_NCCL, "ncclSend/ncclRecv");
       }
@@ -206,33 +253,64 @@ h3c_status h3c_attn_fwd_seqshard(h3c_ctx* ctx, const h3c_attn_args* args, void* 
     if (n->GroupEnd() != 0) return fail(ctx, H3C_ERR_NCCL, "ncclGroupEnd");
     return H3C_OK;
   };
+  auto chunk_of = [&](int c, int* h0, int* hc) {
+    *h0 = c * hp / nchunk;
+    *hc = (c + 1) * hp / nchunk - *h0;
+  };
+  auto send_out = [&](int c) -> h3c_status {
+    int h0, hc;
+    chunk_of(c, &h0, &hc);
+    const size_t off = (size_t)P * s_r * h0 * 128, per_peer = (size_t)s_r * hc * 128;
+    H3_CUDA_TRY(ctx, cudaStreamWaitEvent(x, st->attn_done[c], 0));
+    h3c_status e = exchange(ox + off, send + off, per_peer);
+    if (e != H3C_OK) return e;
+    pack_kernel<<<blocks, threads, 0, x>>>((uint16_t*)a.out.ptr, a.out.token_stride, a.out.head_stride, send + off,
+                                           s_r, P, hp, h0, hc, 1);
+    H3_CUDA_TRY(ctx, cudaGetLastError());
+    return H3C_OK;
+  };
+
+  H3_CUDA_TRY(ctx, cudaEventRecord(st->start, s));
+  H3_CUDA_TRY(ctx, cudaStreamWaitEvent(x, st->start, 0));
   const h3c_view ins[3] = {a.q, a.k, a.v};
   uint16_t* outs[3] = {qx, kx, vx};
-  for (int i = 0; i < 3; ++i) {
-    pack_kernel<<<blocks, threads, 0, s>>>((uint16_t*)ins[i].ptr, ins[i].token_stride, ins[i].head_stride, send, s_r,
-                                           a.heads, hp, 0);
-    H3_CUDA_TRY(ctx, cudaGetLastError());
-    h3c_status e = exchange(send, outs[i]);
+  for (int c = 0; c < nchunk; ++c) {
+    int h0, hc;
+    chunk_of(c, &h0, &hc);
+    const size_t off = (size_t)P * s_r * h0 * 128, per_peer = (size_t)s_r * hc * 128;
+    for (int i = 0; i < 3; ++i) {
+      pack_kernel<<<blocks, threads, 0, x>>>((uint16_t*)ins[i].ptr, ins[i].token_stride, ins[i].head_stride,
+                                             send + off, s_r, P, hp, h0, hc, 0);
+      H3_CUDA_TRY(ctx, cudaGetLastError());
+      h3c_status e = exchange(send + off, outs[i] + off, per_peer);
+      if (e != H3C_OK) return e;
+    }
+    H3_CUDA_TRY(ctx, cudaEventRecord(st->in_done[c], x));
+    // the previous chunk's output goes back once its attention is done
+    if (c > 0) {
+      h3c_status e = send_out(c - 1);
+      if (e != H3C_OK) return e;
+    }
+    // the fused call on [P * S_r, hc, D]: every token, this chunk's heads
+    H3_CUDA_TRY(ctx, cudaStreamWaitEvent(s, st->in_done[c], 0));
+    h3c_attn_args la = a;
+    const int64_t ts = (int64_t)hc * 128;
+    la.q = h3c_view{qx + off, ts, 128};
+    la.k = h3c_view{kx + off, ts, 128};
+    la.v = h3c_view{vx + off, ts, 128};
+    la.out = h3c_view{ox + off, ts, 128};
+    la.heads = hc;
+    la.head_offset = 0;
+    la.head_count = hc;
+    h3c_status e = h3c_attn_fwd(ctx, &la, stream);
     if (e != H3C_OK) return e;
+    H3_CUDA_TRY(ctx, cudaEventRecord(st->attn_done[c], s));
   }
-  // the fused call on [P * S_r, H/P, D]: every token, this rank's heads
-  h3c_attn_args la = a;
-  const int64_t ts = (int64_t)hp * 128;
-  la.q = h3c_view{qx, ts, 128};
-  la.k = h3c_view{kx, ts, 128};
-  la.v = h3c_view{vx, ts, 128};
-  la.out = h3c_view{ox, ts, 128};
-  la.heads = hp;
-  la.head_offset = 0;
-  la.head_count = hp;
-  h3c_status e = h3c_attn_fwd(ctx, &la, stream);
+  h3c_status e = send_out(nchunk - 1);
   if (e != H3C_OK) return e;
   // rows past seq_len are not computed; they come back as unspecified padding
-  e = exchange(ox, send);
-  if (e != H3C_OK) return e;
-  pack_kernel<<<blocks, threads, 0, s>>>((uint16_t*)a.out.ptr, a.out.token_stride, a.out.head_stride, send, s_r,
-                                         a.heads, hp, 1);
-  H3_CUDA_TRY(ctx, cudaGetLastError());
+  H3_CUDA_TRY(ctx, cudaEventRecord(st->out_done, x));
+  H3_CUDA_TRY(ctx, cudaStreamWaitEvent(s, st->out_done, 0));
   return H3C_OK;
 }
 
