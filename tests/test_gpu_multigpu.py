@@ -75,7 +75,7 @@ def test_ulysses_two_gpus_matches_single_gpu(gpu):
         assert err == 0.0, (rank, err)  # same kernels, same per-head inputs
 
 
-def _abi_worker(rank, world, id_q, q_out):
+def _abi_worker(rank, world, id_q, q_out, chunks=1):
     try:
         _abi_body(rank, world, id_q, q_out)
     except Exception as e:  # report instead of leaving the parent waiting
@@ -88,6 +88,7 @@ def _abi_body(rank, world, id_q, q_out):
     root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
     sys.path[:0] = [root, os.path.join(root, "minimax-h3-swift_b200")]
     os.environ["NCCL_NVLS_ENABLE"] = "0"
+    os.environ["H3C_SEQ_CHUNKS"] = str(chunks)
     import torch
 
     from h3attention import BlockList, Runtime
@@ -123,9 +124,11 @@ def _abi_body(rank, world, id_q, q_out):
     q_out.put((rank, (out[: hi - lo].float() - want[lo:hi].float()).abs().max().item()))
 
 
-def test_c_abi_seqshard_two_gpus(gpu):
+@pytest.mark.parametrize("chunks", [1, 3])
+def test_c_abi_seqshard_two_gpus(gpu, chunks):
     """h3c_comm_init + h3c_attn_fwd_seqshard (NCCL grouped send/recv inside
-    the library) on 2 GPUs equals the single-GPU fused call."""
+    the library) on 2 GPUs equals the single-GPU fused call, unpipelined and
+    pipelined over 3 uneven head chunks (4 heads per rank)."""
     import torch
     import torch.multiprocessing as mp
 
@@ -133,7 +136,7 @@ def test_c_abi_seqshard_two_gpus(gpu):
         pytest.skip("needs 2 GPUs")
     ctx = mp.get_context("spawn")
     q, id_q = ctx.Queue(), ctx.Queue()
-    procs = [ctx.Process(target=_abi_worker, args=(r, 2, id_q, q)) for r in range(2)]
+    procs = [ctx.Process(target=_abi_worker, args=(r, 2, id_q, q, chunks)) for r in range(2)]
     for p in procs:
         p.start()
     try:
