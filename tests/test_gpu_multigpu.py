@@ -77,12 +77,12 @@ def test_ulysses_two_gpus_matches_single_gpu(gpu):
 
 def _abi_worker(rank, world, id_q, q_out, chunks=1):
     try:
-        _abi_body(rank, world, id_q, q_out)
+        _abi_body(rank, world, id_q, q_out, chunks)
     except Exception as e:  # report instead of leaving the parent waiting
         q_out.put((rank, repr(e)))
 
 
-def _abi_body(rank, world, id_q, q_out):
+def _abi_body(rank, world, id_q, q_out, chunks):
     import sys
 
     root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
