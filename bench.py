@@ -310,7 +310,13 @@ def run_ours(args):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
     value = job_flops / (ms * 1e-3) / 1e12
-    launches = 3 * args.steps  # K prologue, Q prologue, attention per call
+    # our kernels per call: K prologue, Q prologue, attention; the C-ABI
+    # sequence-sharded call adds, per head chunk, 3 packs and 1 unpack
+    if mode == "seq":
+        chunks = min(H // ws, max(1, int(os.environ.get("H3C_SEQ_CHUNKS", "1"))))
+        launches = chunks * (3 + 3 + 1) * args.steps
+    else:
+        launches = 3 * args.steps
 
     # Roofline pass: the attention kernel alone on pre-normalised Q/K, each
     # launch bracketed by events on the launching stream.
