@@ -502,16 +502,17 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int c = 0; c < 128; ++c)
               if (c >= valid) s[c] = __float_as_uint(-INFINITY);
           }
-          float mxa[4];
+          // row max: 8 independent chains of 16 (short dependency chains)
+          float mxa[8];
 #pragma unroll
-          for (int g = 0; g < 4; ++g) {
-            float r = __uint_as_float(s[32 * g]);
+          for (int g = 0; g < 8; ++g) {
+            float r = __uint_as_float(s[16 * g]);
 #pragma unroll
-            for (int c = 1; c < 31; c += 2)
-              r = max3(r, __uint_as_float(s[32 * g + c]), __uint_as_float(s[32 * g + c + 1]));
-            mxa[g] = fmaxf(r, __uint_as_float(s[32 * g + 31]));
+            for (int c = 1; c < 15; c += 2)
+              r = max3(r, __uint_as_float(s[16 * g + c]), __uint_as_float(s[16 * g + c + 1]));
+            mxa[g] = fmaxf(r, __uint_as_float(s[16 * g + 15]));
           }
-          const float mx = max3(mxa[0], mxa[1], fmaxf(mxa[2], mxa[3]));
+          const float mx = max3(max3(mxa[0], mxa[1], mxa[2]), max3(mxa[3], mxa[4], mxa[5]), fmaxf(mxa[6], mxa[7]));
           const float mxs = mx * sl2;
           // Lazy rescale: keep the running max unless the new one exceeds it
           // by more than 8 (a factor 256 in the exponentials).
