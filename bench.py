@@ -206,7 +206,7 @@ def run_reference(args):
 # dram__bytes_write.sum), from the ncu capture summarised in
 # profiles/attn_tc_kernel_config2.md (captured at 8 heads, scaled by 40/8);
 # None for workloads without a capture.
-TRAFFIC_BYTES = {"config2": 5.94e9}
+TRAFFIC_BYTES = {"config2": 5.92e9}
 
 
 def _timed(fn, steps):
