@@ -186,10 +186,11 @@ typedef struct { int32_t start, stop, kind; } h3c_segment;
 
 /* Segment table and total rows of the packed sequence (host only).  An
  * anchor off the timeline or an axis smaller than the patch is refused with
- * H3C_ERR_INVALID_ARGUMENT (the reference throws H3Error there).  capacity 0
- * queries the counts; a smaller non-zero capacity returns H3C_ERR_CAPACITY. */
+ * H3C_ERR_INVALID_ARGUMENT and the reason in err (the reference throws
+ * H3Error there; err may be NULL).  capacity 0 queries the counts; a smaller
+ * non-zero capacity returns H3C_ERR_CAPACITY. */
 h3c_status h3c_packed_layout(const h3c_layout_spec* spec, h3c_segment* segments, int32_t capacity,
-                             int32_t* n_segments, int64_t* total_tokens);
+                             int32_t* n_segments, int64_t* total_tokens, char* err, size_t err_len);
 /* d_pos [S, 3] fp32 = Float(positionIds), bit-identical to the reference's
  * float64 construction narrowed to fp32.  capacity in tokens.  At most 40
  * segments.  Stream-ordered, no allocation. */

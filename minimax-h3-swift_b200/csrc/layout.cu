@@ -16,6 +16,7 @@
 // contraction into FMA), so the fp32 positions are bit-identical to the
 // reference's Float(Double) narrowing.
 #include <math.h>
+#include <string.h>
 
 #include <vector>
 
@@ -260,11 +261,20 @@ h3c_status fail_layout(h3c_ctx* ctx, h3c_status st, const std::string& msg) {
 extern "C" {
 
 h3c_status h3c_packed_layout(const h3c_layout_spec* spec, h3c_segment* segments, int32_t capacity,
-                             int32_t* n_segments, int64_t* total_tokens) {
-  if (!spec || !n_segments || !total_tokens || capacity < 0 || (capacity && !segments)) return H3C_ERR_INVALID_ARGUMENT;
+                             int32_t* n_segments, int64_t* total_tokens, char* err, size_t err_len) {
+  auto refuse = [&](const std::string& msg) {
+    if (err && err_len) {
+      const size_t m = msg.size() < err_len - 1 ? msg.size() : err_len - 1;
+      memcpy(err, msg.data(), m);
+      err[m] = 0;
+    }
+    return H3C_ERR_INVALID_ARGUMENT;
+  };
+  if (!spec || !n_segments || !total_tokens || capacity < 0 || (capacity && !segments))
+    return refuse("h3c_packed_layout: null or negative argument");
   h3::Built b;
   std::string e = h3::build_layout(*spec, &b);
-  if (!e.empty()) return H3C_ERR_INVALID_ARGUMENT;
+  if (!e.empty()) return refuse(e);
   *n_segments = (int32_t)b.segments.size();
   *total_tokens = b.dev.total;
   if (capacity && capacity < (int32_t)b.segments.size()) return H3C_ERR_CAPACITY;

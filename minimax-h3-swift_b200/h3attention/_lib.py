@@ -132,7 +132,8 @@ def load() -> C.CDLL:
             "h3c_blockmask_build_device": ([vp, C.POINTER(MaskSpec), vp, vp, i64, C.POINTER(i64), vp], st),
             "h3c_rope_table": ([vp, vp, i32, C.POINTER(i32), f64, vp, vp], st),
             "h3c_rope_table_shared": ([vp, vp, i32, vp, i32, vp, vp], st),
-            "h3c_packed_layout": ([C.POINTER(LayoutSpec), C.POINTER(Segment), i32, C.POINTER(i32), C.POINTER(i64)], st),
+            "h3c_packed_layout": ([C.POINTER(LayoutSpec), C.POINTER(Segment), i32, C.POINTER(i32), C.POINTER(i64),
+                                   C.c_char_p, C.c_size_t], st),
             "h3c_packed_positions_device": ([vp, C.POINTER(LayoutSpec), vp, i64, vp], st),
             "h3c_rope_table_layout": ([vp, C.POINTER(LayoutSpec), vp, i32, vp, i64, vp], st),
             "h3c_prologue": ([vp, View, View, i32, i32, i32, i32, vp, f32, vp, i32, vp], st),

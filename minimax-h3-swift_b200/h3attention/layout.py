@@ -87,13 +87,13 @@ class PackedLayout:
         spec = self.spec()
         n_seg, total = C.c_int32(0), C.c_int64(0)
         L = _lib.load()
-        st = L.h3c_packed_layout(C.byref(spec), None, 0, C.byref(n_seg), C.byref(total))
+        err = C.create_string_buffer(256)
+        st = L.h3c_packed_layout(C.byref(spec), None, 0, C.byref(n_seg), C.byref(total), err, 256)
         if st == _lib.H3C_ERR_INVALID_ARGUMENT:
-            raise LayoutError(f"layout refused: text={self.text_tokens} {self.geometry} keyframes={list(self.keyframes)} "
-                              f"refs={list(self.refs)}")
+            raise LayoutError(err.value.decode())
         _lib.check(st, what="h3c_packed_layout")
         segs = (_lib.Segment * max(1, n_seg.value))()
-        _lib.check(L.h3c_packed_layout(C.byref(spec), segs, n_seg.value, C.byref(n_seg), C.byref(total)),
+        _lib.check(L.h3c_packed_layout(C.byref(spec), segs, n_seg.value, C.byref(n_seg), C.byref(total), None, 0),
                    what="h3c_packed_layout")
         self.segments = [(s.start, s.stop, SEGMENT_KINDS[s.kind]) for s in segs[:n_seg.value]]
         self.total_tokens = total.value

@@ -71,8 +71,9 @@ package final class CUDABackend: H3AttentionBackend, @unchecked Sendable {
         var spec = layout
         var nseg: Int32 = 0
         var total: Int64 = 0
-        guard h3c_packed_layout(&spec, nil, 0, &nseg, &total) == H3C_OK else {
-            throw H3Error.unavailableFeature(feature: "b200 rope table", detail: "layout refused")
+        var err = [CChar](repeating: 0, count: 256)
+        guard h3c_packed_layout(&spec, nil, 0, &nseg, &total, &err, err.count) == H3C_OK else {
+            throw H3Error.unavailableFeature(feature: "b200 rope table", detail: String(cString: err))
         }
         ropeTable = cudaMallocBridge(Int(total) * Int(3 * n) * 8)
         guard let ctx, h3c_rope_table_layout(ctx, &spec, invFreq, n, ropeTable, total, nil) == H3C_OK else {

@@ -48,7 +48,11 @@ static void render(h3c_layout_spec* spec, int32_t* keyframe) {
 static int mask_for(const h3c_layout_spec* spec, h3c_mask_spec* m, int64_t* total) {
   h3c_segment seg[8];
   int32_t nseg = 0;
-  if (h3c_packed_layout(spec, seg, 8, &nseg, total) != H3C_OK) return 1;
+  char err[256];
+  if (h3c_packed_layout(spec, seg, 8, &nseg, total, err, sizeof(err)) != H3C_OK) {
+    fprintf(stderr, "%s\n", err);
+    return 1;
+  }
   const h3c_segment* video = &seg[nseg - 1];
   if (video->kind != H3C_SEG_VIDEO || video->stop != *total) return 1;
   memset(m, 0, sizeof(*m));

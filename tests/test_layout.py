@@ -136,7 +136,7 @@ def test_library_refusals():
     from h3attention.layout import LayoutError
 
     for bad in (-1, 124):
-        with pytest.raises(LayoutError):
+        with pytest.raises(LayoutError, match="off the timeline"):
             _library_layout(52, (864, 480, 120), [bad], [])
     with pytest.raises(LayoutError):  # a 1-latent-row reference image is off the patch grid
         _library_layout(52, (864, 480, 120), [], [dict(kind="image", latent_h=1, latent_w=16)])
@@ -152,7 +152,7 @@ def test_capacity_query():
     spec = lay.spec()
     n, total = C.c_int32(0), C.c_int64(0)
     small = (_lib.Segment * 2)()
-    st = _lib.load().h3c_packed_layout(C.byref(spec), small, 2, C.byref(n), C.byref(total))
+    st = _lib.load().h3c_packed_layout(C.byref(spec), small, 2, C.byref(n), C.byref(total), None, 0)
     assert st == _lib.H3C_ERR_CAPACITY and n.value == 5 and total.value == lay.total_tokens
 
 
