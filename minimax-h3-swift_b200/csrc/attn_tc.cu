@@ -403,10 +403,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (!ring_wait(item)) return false;
             v_ready = e;
           }
-          const uint32_t vbase = smem_u32(sKV + (item % kStages) * kTileBytes);
+          // descriptors are built once per tile; the start-address field
+          // (bits 0-13, address >> 4) is advanced by plain addition (no
+          // carry: shared addresses stay below 2^18)
+          const uint64_t vdesc = smem_desc(smem_u32(sKV + (item % kStages) * kTileBytes), kHalfBytes, 1024);
 #pragma unroll
           for (int kk = 0; kk < 8; ++kk)
-            mma_ts(tmem + 256 * t + 128, tmem + 256 * t + kk * 8, smem_desc(vbase + kk * 2048, kHalfBytes, 1024),
+            mma_ts(tmem + 256 * t + 128, tmem + 256 * t + kk * 8, vdesc + (uint64_t)((kk * 2048) >> 4),
                    kIdPV, (nst > 1 || kk > 0) ? 1u : 0u);
           pend = -1;
           if (other != e) tc_commit(smem_u32(&bars->kv_empty[item % kStages]));
@@ -414,12 +417,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         };
         auto issue_s = [&](auto tile, int e) {
           constexpr int t = decltype(tile)::value;
-          const uint32_t qa = smem_u32(sQ + t * kTileBytes);
-          const uint32_t kbase = smem_u32(sKV + ((2 * e) % kStages) * kTileBytes);
+          const uint64_t qdesc = smem_desc(smem_u32(sQ + t * kTileBytes), 16, 1024);
+          const uint64_t kdesc = smem_desc(smem_u32(sKV + ((2 * e) % kStages) * kTileBytes), 16, 1024);
 #pragma unroll
           for (int kk = 0; kk < 8; ++kk) {
             const uint32_t off = (kk >> 2) * kHalfBytes + (kk & 3) * 32;
-            mma_ss(tmem + 256 * t, smem_desc(qa + off, 16, 1024), smem_desc(kbase + off, 16, 1024), kIdS,
+            mma_ss(tmem + 256 * t, qdesc + (uint64_t)(off >> 4), kdesc + (uint64_t)(off >> 4), kIdS,
                    kk > 0 ? 1u : 0u);
           }
           tc_commit(smem_u32(&bars->s_full[t]));
