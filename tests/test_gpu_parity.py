@@ -152,6 +152,30 @@ def test_attention_matches_checker(gpu, kernel, name):
 
 
 @pytest.mark.parametrize("kernel", ["mma_sync", "tcgen05"])
+def test_growing_scores_exercise_the_rescale(gpu, kernel):
+    """Keys whose magnitude grows block by block make the row max jump by
+    more than 2^8 several times along a row, so the lazy rescale of O and l
+    (and, in the tcgen05 kernel, the recomputation of a block's
+    exponentials after the max moved) runs on every row."""
+    import torch
+
+    from h3attention import _lib
+
+    S, H = 2048, 2
+    q, k, v, rp, ci = _case(S, H, dict(seq_len=S, prefix_len=S, frames=0, height=0, width=0))
+    kf = O.bf16_to_f32(k).reshape(S // 128, 128, H, 128) * (1.0 + 1.5 * np.arange(S // 128))[:, None, None, None]
+    k = O.f32_to_bf16(kf.reshape(S, H, 128).astype(np.float32))
+    want = O.attend_streaming(q, k, v, rp, ci)
+    qd, kd, vd = (_t(a, gpu) for a in (q, k, v))
+    out = torch.full_like(qd, float("nan"))
+    blocks = (torch.from_numpy(rp).to(gpu), torch.from_numpy(ci).to(gpu))
+    flags = _lib.H3C_KERNEL_MMA_SYNC if kernel == "mma_sync" else 0
+    _rt().attn_fwd(q=qd, k=kd, v=vd, out=out, layout="SHD", scale=1 / np.sqrt(128), blocks=blocks, flags=flags)
+    torch.cuda.synchronize()
+    _check_attn(_np(out), want)
+
+
+@pytest.mark.parametrize("kernel", ["mma_sync", "tcgen05"])
 def test_empty_rows_give_zeros(gpu, kernel):
     """A caller-supplied block list may leave query blocks without any kept
     key block; their rows come out as zeros (O / max(l, 1e-30) with l = 0),
