@@ -229,6 +229,25 @@ def test_fused_prologue_matches_checker(gpu, kernel):
     _check_attn(_np(out), want)
 
 
+def test_fused_norm_without_rope(gpu):
+    """The fused call without a RoPE table (AttentionLayer runs RoPE only when
+    the render has a table, DiTBlock.swift:349-352): RMSNorm alone on q and k
+    (H3C_NO_ROPE), against the checker."""
+    import torch
+
+    S, H = 1500, 3
+    q, k, v, rp, ci = _case(S, H, dict(seq_len=S, frames=15, height=10, width=10, n_random=1, seed=9))
+    wq, wk = (O.fill_normal_bf16((128,), 9, st, 1.0, 0.02) for st in (4, 5))
+    want = O.attend_streaming(O.prologue(q, wq, 1e-6, None), O.prologue(k, wk, 1e-6, None), v, rp, ci)
+    qd, kd, vd = (_t(a, gpu) for a in (q, k, v))
+    out = torch.empty_like(qd)
+    blocks = (torch.from_numpy(rp).to(gpu), torch.from_numpy(ci).to(gpu))
+    _rt().attn_fwd(q=qd, k=kd, v=vd, out=out, layout="SHD", scale=1 / np.sqrt(128), blocks=blocks,
+                   q_norm=_t(wq, gpu), k_norm=_t(wk, gpu), eps=1e-6, rope_table=None)
+    torch.cuda.synchronize()
+    _check_attn(_np(out), want)
+
+
 def test_hsd_layout_and_head_shard(gpu):
     """The seam's [H,S,D] layout, and a head shard [1, 3) of 4 heads."""
     import torch
