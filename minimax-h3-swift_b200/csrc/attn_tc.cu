@@ -315,45 +315,50 @@ __global__ void __launch_bounds__(kThreads, 1)
           tma_load_3d(dst, &tm_q, bar, 0, (qb0 + t) * 128, h);
           tma_load_3d(dst + kHalfBytes, &tm_q, bar, 64, (qb0 + t) * 128, h);
         }
-        int n = 0;
+        // Union entry e: K into ring item 2e, V into item 2e+1, both on the
+        // entry's barrier kv_full[e & 1] (one wait covers K and V).
+        int issued = 0;  // entries whose loads were issued
         bool ok = true;
-        auto load = [&](const CUtensorMap* map, int jb, int info) {
-          const int slot = n % kStages;
-          const uint32_t ph = (uint32_t)((n / kStages) & 1);
-          if (n == a.drop_item) {  // host-side fault injection for tests: this load never happens
-            ++n;
-            return;
-          }
-          if (!mbar_wait(smem_u32(&bars->kv_empty[slot]), ph ^ 1u, abort_flag, a.status, a.wait_limit_ns)) {
+        auto load_entry = [&](int e, int jb, int info) {
+          const int sk = (2 * e) % kStages, sv = (2 * e + 1) % kStages;
+          const uint32_t phk = (uint32_t)(((2 * e) / kStages) & 1), phv = (uint32_t)(((2 * e + 1) / kStages) & 1);
+          if (!mbar_wait(smem_u32(&bars->kv_empty[sk]), phk ^ 1u, abort_flag, a.status, a.wait_limit_ns) ||
+              !mbar_wait(smem_u32(&bars->kv_empty[sv]), phv ^ 1u, abort_flag, a.status, a.wait_limit_ns)) {
             ok = false;
             return;
           }
-          uint32_t bar = smem_u32(&bars->kv_full[slot]);
-          if (info >= 0) bars->info[(n >> 1) & 15] = info;
-          mbar_expect_tx(bar, kTileBytes);
-          uint32_t dst = smem_u32(sKV + slot * kTileBytes);
-          tma_load_3d(dst, map, bar, 0, jb * 128, h);
-          tma_load_3d(dst + kHalfBytes, map, bar, 64, jb * 128, h);
-          ++n;
+          const uint32_t bar = smem_u32(&bars->kv_full[e & 1]);
+          bars->info[e & 15] = info;
+          mbar_expect_tx(bar, 2 * kTileBytes);
+          // host-side fault injection for tests: a dropped item's load never
+          // happens, so its entry never completes
+          if (2 * e != a.drop_item) {
+            const uint32_t dst = smem_u32(sKV + sk * kTileBytes);
+            tma_load_3d(dst, &tm_k, bar, 0, jb * 128, h);
+            tma_load_3d(dst + kHalfBytes, &tm_k, bar, 64, jb * 128, h);
+          }
+          if (2 * e + 1 != a.drop_item) {
+            const uint32_t dst = smem_u32(sKV + sv * kTileBytes);
+            tma_load_3d(dst, &tm_v, bar, 0, jb * 128, h);
+            tma_load_3d(dst + kHalfBytes, &tm_v, bar, 64, jb * 128, h);
+          }
+          issued = e + 1;
         };
         int i0 = 0, i1 = 0;
-        while (ok && (i0 < tn[0] || i1 < tn[1])) {
+        for (int e = 0; ok && (i0 < tn[0] || i1 < tn[1]); ++e) {
           const int c0 = i0 < tn[0] ? a.col_idx[tp0[0] + i0] : INT_MAX;
           const int c1 = i1 < tn[1] ? a.col_idx[tp0[1] + i1] : INT_MAX;
           const int u = min(c0, c1);
           i0 += (c0 == u);
           i1 += (c1 == u);
           const bool last = i0 >= tn[0] && i1 >= tn[1];
-          load(&tm_k, u, (c0 == u ? 1 : 0) | (c1 == u ? 2 : 0) | (last ? 4 : 0));
-          if (ok) load(&tm_v, u, -1);
+          load_entry(e, u, (c0 == u ? 1 : 0) | (c1 == u ? 2 : 0) | (last ? 4 : 0));
         }
         // Drain: wait for the last loads to land before anyone may exit.
         if (!ok) {
-          for (int m = (n > kStages ? n - kStages : 0); m < n; ++m) {
-            const int slot = m % kStages;
-            const uint32_t ph = (uint32_t)((m / kStages) & 1);
+          for (int m = (issued > 2 ? issued - 2 : 0); m < issued; ++m) {
             volatile int32_t zero = 0;
-            mbar_wait(smem_u32(&bars->kv_full[slot]), ph, &zero, nullptr);
+            mbar_wait(smem_u32(&bars->kv_full[m & 1]), (uint32_t)((m >> 1) & 1), &zero, nullptr);
           }
         }
       }
@@ -379,13 +384,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         // issue path).
         int pend0 = -1, pend1 = -1;  // union entry whose PV is still due, per tile
         int ns0 = 0, ns1 = 0;        // S issued per tile
-        int v_ready = -1;            // union entry whose V tile is known to have landed
-        auto ring_wait = [&](int item) -> bool {
-          const int slot = item % kStages;
-          if (!mbar_wait(smem_u32(&bars->kv_full[slot]), (uint32_t)((item / kStages) & 1), abort_flag, a.status,
+        int landed = -1;  // last union entry whose K and V are known to have landed
+        auto wait_entry = [&](int e) -> bool {
+          if (e <= landed) return true;
+          if (!mbar_wait(smem_u32(&bars->kv_full[e & 1]), (uint32_t)((e >> 1) & 1), abort_flag, a.status,
                          a.wait_limit_ns))
             return false;
           tc_fence_after();
+          landed = e;
           return true;
         };
         auto issue_pv = [&](auto tile) -> bool {
@@ -399,10 +405,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             return false;
           tc_fence_after();
           const int item = 2 * e + 1;
-          if (v_ready != e) {
-            if (!ring_wait(item)) return false;
-            v_ready = e;
-          }
+          if (!wait_entry(e)) return false;
           // descriptors are built once per tile; the start-address field
           // (bits 0-13, address >> 4) is advanced by plain addition (no
           // carry: shared addresses stay below 2^18)
@@ -435,7 +438,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // memory, so this thread issues no global loads.
         for (int e = 0; ok; ++e) {
           if (pend0 >= 0) ok = issue_pv(T0{});
-          if (!ok || !ring_wait(2 * e)) {
+          if (!ok || !wait_entry(e)) {
             ok = false;
             break;
           }
