@@ -11,9 +11,12 @@
 // CTA walks the union of the two lists and every K/V tile it loads serves
 // both query tiles: half the L2->SM traffic of one query block per CTA.
 // Roles:
-//   warp 0      TMA producer: Q tiles once, then K/V of each union entry into
-//               a 4-slot ring
-//   warp 1      MMA issuer (one elected thread): S = Q K^T (SS), O += P V (TS)
+//   warp 0      TMA producer: Q tiles once, then K and V of each union entry
+//               into a 4-slot ring (two entries; an entry's K and V complete
+//               one barrier), handing the entry's tile flags to the issuer
+//   warp 1      MMA issuer (one elected thread): S = Q K^T (SS), O += P V (TS),
+//               in the order PV0 S0 PV1 S1 per entry so the two tiles'
+//               softmax phases alternate
 //   warp 2      TMEM allocator (512 columns)
 //   warps 4-7   softmax + epilogue of tile 0 (thread = query row = TMEM lane)
 //   warps 8-11  softmax + epilogue of tile 1
@@ -30,8 +33,8 @@
 #include <cuda.h>
 
 #include <climits>
-#include <type_traits>
 #include <cstdlib>
+#include <type_traits>
 
 #include "common.cuh"
 
@@ -46,7 +49,7 @@ constexpr uint64_t kWaitLimitNs = 4000000000ull;  // 4 s
 
 struct __align__(8) Barriers {
   uint64_t q_full[2];
-  uint64_t kv_full[kStages];
+  uint64_t kv_full[kStages];   // [0..1]: entry barriers (K and V of entry e on kv_full[e & 1])
   uint64_t kv_empty[kStages];
   uint64_t s_full[2];
   uint64_t p_full[2];
@@ -54,8 +57,8 @@ struct __align__(8) Barriers {
   uint32_t tmem_base;
   int32_t abort;
   // union entry e: bit 0 tile 0 active, bit 1 tile 1 active, bit 2 last
-  // entry; written by the producer before the arrival that completes
-  // kv_full of K(e), read by the MMA issuer after waiting on it
+  // entry; written by the producer before the arrival on entry e's barrier,
+  // read by the MMA issuer after waiting on it
   int32_t info[16];
 };
 static_assert(sizeof(Barriers) <= 256, "barrier block");
