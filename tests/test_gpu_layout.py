@@ -83,11 +83,15 @@ def test_production_shape_fused(gpu):
                             q_norm=dev(wq), k_norm=dev(wk), eps=1e-5, rope_table=tab_d)
     torch.cuda.synchronize()
     got = O.bf16_to_f32(out.cpu().view(torch.int16).numpy().view(np.uint16)).transpose(1, 0, 2)
-    rows = np.concatenate([np.arange(b * 128, min(S, b * 128 + 128)) for b in qbs])
-    for h in heads:
-        err = np.abs(got[h, rows] - want[h, rows])
-        assert np.isfinite(got[h, rows]).all()
-        assert err.max() <= 2e-2 and err.mean() <= 2e-3, (h, err.max(), err.mean())
+    sampled = np.zeros(S, bool)
+    for b in qbs:
+        sampled[b * 128:min(S, b * 128 + 128)] = True
+    for a, b, kind in lay.segments:  # per span (text, audio, video), never averaged across them
+        rows = np.nonzero(sampled[a:b])[0] + a
+        for h in heads:
+            err = np.abs(got[h, rows] - want[h, rows])
+            assert np.isfinite(got[h, rows]).all()
+            assert err.max() <= 2e-2 and err.mean() <= 2e-3, (kind, h, err.max(), err.mean())
 
 
 def test_render_through_the_seam(gpu):
@@ -111,7 +115,8 @@ def test_render_through_the_seam(gpu):
     wq, wk = (O.fill_normal_bf16((128,), 41, st, 1.0, 0.02) for st in (4, 5))
     _, pos = O.packed_layout(332, O.latent_geometry(864, 480, 120), [0])
     tab = O.rope_table_shared(pos.astype(np.float32), inv)
-    qbs = [0, 3, 6, 40, bl.n_blocks - 1]
+    # a sample of query blocks covering every span of the packed sequence
+    qbs = sorted({a // 128 for a, b, k in lay.segments if b > a} | {40, bl.n_blocks - 1})
     want = O.attend_streaming(O.prologue(q, wq, 1e-5, tab), O.prologue(k, wk, 1e-5, tab), v, bl.row_ptr,
                               bl.col_idx, qblocks=qbs)
 
@@ -127,7 +132,16 @@ def test_render_through_the_seam(gpu):
     assert out is not None
     torch.cuda.synchronize()
     got = O.bf16_to_f32(out.cpu().view(torch.int16).numpy().view(np.uint16))
-    rows = np.concatenate([np.arange(b * 128, min(S, b * 128 + 128)) for b in qbs])
-    err = np.abs(got[:, rows] - want[:, rows])
-    assert np.isfinite(got[:, rows]).all()
-    assert err.max() <= 2e-2 and err.mean() <= 2e-3, (err.max(), err.mean())
+    sampled = np.zeros(S, bool)
+    for b in qbs:
+        sampled[b * 128:min(S, b * 128 + 128)] = True
+    # error per span, never averaged across spans (the reference's rule,
+    # Tests/H3AttentionTests/AxialMeasureTests.swift:20-27): the prefix rows
+    # are a few percent of the sequence and would vanish in a global mean
+    for a, b, kind in lay.segments:
+        rows = np.nonzero(sampled[a:b])[0] + a
+        if len(rows) == 0:
+            continue
+        err = np.abs(got[:, rows] - want[:, rows])
+        assert np.isfinite(got[:, rows]).all(), kind
+        assert err.max() <= 2e-2 and err.mean() <= 2e-3, (kind, err.max(), err.mean())
