@@ -376,9 +376,6 @@ h3c_status h3c_attn_fwd(h3c_ctx* ctx, const h3c_attn_args* args, void* stream) {
   // skips, so that the consumers' bounded waits run out, and a shorter bound.
   if (const char* d = getenv("H3C_TEST_DROP_ITEM")) L.drop_item = atoi(d);
   if (const char* w = getenv("H3C_TEST_WAIT_LIMIT_NS")) L.wait_limit_ns = strtoull(w, nullptr, 10);
-#ifdef H3_TRACE
-  if (const char* tb = getenv("H3C_TRACE_BUF")) L.trace = (long long*)strtoull(tb, nullptr, 0);
-#endif
   cudaError_t e;
   if (a.flags & H3C_KERNEL_MMA_SYNC) {
     e = h3::launch_attn_mma(L, s);
