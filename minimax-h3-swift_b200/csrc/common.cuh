@@ -78,7 +78,6 @@ struct AttnLaunch {
   int32_t* status;                // device status word (bounded waits), may be null
   uint64_t wait_limit_ns;         // bound of every mbarrier wait
   int32_t drop_item;              // test hook: K/V ring item the producer skips (-1: none)
-  long long* trace;               // phase timestamps (builds with -DH3_TRACE only), may be null
 };
 
 cudaError_t launch_attn_mma(const AttnLaunch& a, cudaStream_t s);
