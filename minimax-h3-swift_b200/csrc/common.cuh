@@ -43,12 +43,6 @@ __device__ __forceinline__ uint16_t f2bf(float f) {
 
 __device__ __forceinline__ float rbf(float f) { return bf2f(f2bf(f)); }
 
-// The RMSNorm + split-half RoPE of one 128-wide row held as x[0..127] (fp32
-// values of bf16 inputs) by one thread: y = bf16(x * rsqrt(mean(x^2)+eps) * w),
-// then ra = bf16(bf16(c*a) + bf16(-s*b)), rb = bf16(bf16(s*a) + bf16(c*b)).
-// Used by the fused tcgen05 Q path; the standalone prologue kernel computes
-// the same arithmetic with a warp per row.
-
 }  // namespace h3
 
 #define H3_CUDA_TRY(ctx, expr)                                                   \
@@ -73,8 +67,6 @@ struct AttnLaunch {
   float scale_log2;               // scale * log2(e)
   const int32_t* row_ptr;
   const int32_t* col_idx;
-  // fused Q prologue (tcgen05 path only); q_norm == nullptr means q is final
-  const uint16_t* q_norm; const uint16_t* rope; int32_t rope_half; float eps;
   int32_t* status;                // device status word (bounded waits), may be null
   uint64_t wait_limit_ns;         // bound of every mbarrier wait
   int32_t drop_item;              // test hook: K/V ring item the producer skips (-1: none)
