@@ -10,8 +10,16 @@ larger than L2 (no flush needed).
   python bench.py [--gpus N] [--steps K] [--warmup W] [--config config2]
   python bench.py --impl reference ...   # the CPU restatement on host cores
 
-Multi-GPU (torchrun, one rank per GPU): every rank runs its own full call
-(weak scaling, no data-path collective); time = max over ranks.
+Multi-GPU (torchrun, one rank per GPU): by default the heads are split
+across the ranks (contiguous head ranges, one fused call per rank, no
+data-path collective: the block list is the same for every head), value =
+the whole job's FLOPs / the max over ranks of the call time (strong
+scaling).  --mode seq / seq_torch run the sequence-sharded layout (NCCL
+all-to-alls, strong scaling); --mode replica runs a full call per rank (weak).
+
+After the timed region every rank checks its own output on sampled query
+blocks and heads against a plain PyTorch fp32 restatement of the op
+(h3attention.torchref); rank 0 prints the per-rank errors under "parity".
 """
 import argparse
 import json
@@ -101,35 +109,56 @@ def _dist():
     return ws, rank, local
 
 
-def _workload(name, heads=None):
+def _workload(name, heads=None, build=None):
+    """The named workload; ``build`` (spec -> BlockList) is the block-list
+    builder config 5's density calibration uses (the library's by default)."""
     from h3attention.configs import CONFIGS, config5
 
     from dataclasses import replace
 
-    wl = config5(float(name.split("@")[1])) if name.startswith("config5@") else CONFIGS[name]
+    wl = config5(float(name.split("@")[1]), build=build) if name.startswith("config5@") else CONFIGS[name]
     if heads:
         wl = replace(wl, heads=heads, name=f"{wl.name}/h{heads}")
     return wl
+
+
+def _oracle_blocklist(spec):
+    """The block list built by the CPU restatement (oracle/), as a BlockList
+    (host arrays only; the library is not loaded)."""
+    from dataclasses import asdict
+
+    from h3attention.blockmask import BlockList
+    from oracle import oracle as O
+
+    rp, ci = O.blockmask_build(O.mask_spec(**asdict(spec)))
+    return BlockList(spec.seq_len, rp, ci, spec.block)
+
+
+def _host_cores():
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
 
 
 class CpuBaseline:
     """The CPU restatement (oracle/, kind "port": the reference's Swift/MLX
     path cannot run on Linux) timed on this host: prologue + streaming
     attention over a deterministic sample of query blocks of the benchmark's
-    block list, every host core, extrapolated by counted kept-pair FLOPs."""
+    block list (built by the restatement itself), on every host core whatever
+    OMP_NUM_THREADS says, extrapolated to the whole call by counted kept-pair
+    FLOPs."""
 
-    def __init__(self, wl, cores=None):
+    def __init__(self, wl):
         import numpy as np
 
-        from h3attention import BlockList
         from oracle import oracle as O
 
         self.O, self.np, self.wl = O, np, wl
         L = O.lib()
-        if cores:
-            L.h3o_set_num_threads(cores)
+        L.h3o_set_num_threads(_host_cores())
         self.threads = L.h3o_num_threads()
-        self.bl = BlockList.build(wl.mask_spec())
+        self.bl = _oracle_blocklist(wl.mask_spec())
         self.H = min(wl.heads, 2)
         S, H = wl.seq_len, self.H
         self.order = np.random.default_rng(7).permutation(self.bl.n_blocks)
@@ -169,43 +198,70 @@ class CpuBaseline:
         attn_full = elapsed * bl.flops(wl.heads) / done_flops
         ms = (pro_full + attn_full) * 1e3
         return {"value": bl.flops(wl.heads) / (ms * 1e-3) / 1e12, "unit": "TFLOP/s", "cores": self.threads,
-                "kind": "port", "ms_per_call": ms,
+                "kind": "port", "ms_per_call": ms, "extrapolated": True, "measured_s": elapsed + pro_s,
                 "sample": f"{used} of {nb} query blocks x {H} of {wl.heads} heads ({elapsed:.1f} s attention, "
-                          f"{pro_s:.1f} s prologue of {H} heads), extrapolated by kept-pair FLOPs"}
+                          f"{pro_s:.1f} s prologue of {H} heads, {self.threads} threads), extrapolated to one "
+                          f"whole call by kept-pair FLOPs"}
+
+
+def _config(wl, bl, ws, mode):
+    """The workload description both arms print (identical dicts)."""
+    return {"workload": wl.name, "seq_len": wl.seq_len, "heads": wl.heads, "head_dim": 128, "block": 128,
+            "density": round(bl.density, 4), "kept_blocks": bl.nnz, "flops_per_call": bl.flops(wl.heads),
+            "l2": "inputs larger than L2 (no flush)",
+            "parallelism": {"replica": f"replicas x{ws} (weak)", "heads": f"head-sharded x{ws}",
+                            "seq": f"sequence-sharded x{ws} (NCCL all-to-alls, C ABI)",
+                            "seq_torch": f"sequence-sharded x{ws} (torch all_to_all_single)"}[mode],
+            "prologue": (f"fused RMSNorm (eps {wl.eps:g}) + RoPE from the packed layout (rot 96, shared "
+                         "inv_freq)" if wl.render else
+                         f"fused RMSNorm (eps {wl.eps:g}) + RoPE (t/h/w 32/48/48, theta 1e4)")}
+
+
+def _mode(args, ws):
+    if ws == 1:
+        return "replica"
+    return args.mode or "heads"
 
 
 def run_reference(args):
+    """The reference arm: the CPU restatement of the path on this host's cores
+    (nothing of the library is loaded), on the same workload and config
+    dict as the GPU arm.  Each step is a bounded sample of the call,
+    extrapolated to one whole call (labelled so in the line)."""
     ws, rank, _ = _dist()
     if rank != 0:
         return 0
-    wl = _workload(args.config, args.heads)
-    from h3attention import BlockList
-
-    bl = BlockList.build(wl.mask_spec())
+    wl = _workload(args.config, args.heads, build=_oracle_blocklist)
+    bl = _oracle_blocklist(wl.mask_spec())
     base = CpuBaseline(wl)
     budget = max(2.0, args.ref_budget / (args.warmup + args.steps))
-    vals, cb = [], None
+    vals, cb, measured = [], None, 0.0
     for i in range(args.warmup + args.steps):
         cb = base.sample(budget)
         if i >= args.warmup:
             vals.append(cb["value"])
+            measured += cb["measured_s"]
     v = statistics.median(vals)
     ms = bl.flops(wl.heads) / (v * 1e12) * 1e3
     line = {"metric": METRIC, "value": v, "unit": "TFLOP/s", "n_gpus": ws, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "impl": "reference",
-            "config": {"workload": wl.name, "seq_len": wl.seq_len, "heads": wl.heads, "head_dim": 128,
-                       "density": bl.density},
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "weak" if _mode(args, ws) == "replica" else "strong",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1) bf16; shapes of the workload)",
+            "impl": "reference", "config": _config(wl, bl, ws, _mode(args, ws)),
+            "extrapolated": True,
+            "timing": f"each step times a sample of the call for about {budget:.0f} s on {base.threads} host "
+                      f"threads and extrapolates it to one whole call; ms_per_step is that extrapolated call "
+                      f"time ({measured:.1f} s measured over the {args.steps} timed steps)",
             "cpu_baseline": {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")},
             "e2e": {"value": v, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
     return 0
 
 
-# Per-launch DRAM traffic of attn_tc_kernel on config2 (dram__bytes_read.sum +
-# dram__bytes_write.sum), from the ncu capture summarised in
-# profiles/attn_tc_kernel_config2.md (captured at 8 heads, scaled by 40/8);
-# None for workloads without a capture.
+# Per-launch DRAM traffic of attn_tc_kernel (dram__bytes_read.sum +
+# dram__bytes_write.sum) from one ncu capture of the config-2 workload at 8
+# heads, scaled to 40 heads by the heads processed; None for workloads
+# without a capture.
 TRAFFIC_BYTES = {"config2": 5.92e9}
 
 
@@ -219,6 +275,73 @@ def _timed(fn, steps):
     e1.record()
     torch.cuda.synchronize()
     return e0.elapsed_time(e1) / steps
+
+
+PARITY_TOL = (2e-2, 2e-3)  # max-abs, mean-abs on bf16 outputs of unit-variance inputs
+
+
+def _parity(mode, ws, rank, wl, bl, q, k, v, out, wq, wk, tab, scale, dev):
+    """Every rank checks its own output of the last timed call on sampled
+    query blocks of one or two of its heads against the plain PyTorch fp32
+    restatement (h3attention.torchref), outside the timed region.  In the
+    sequence-sharded modes the checked head's token shards are gathered
+    first.  Returns rank 0's summary of all ranks (None on other ranks)."""
+    import torch
+    import torch.distributed as dist
+
+    from h3attention import torchref
+
+    S, H = wl.seq_len, wl.heads
+    nb = bl.n_blocks
+    seqm = mode in ("seq", "seq_torch")
+
+    def check(qh, kh, vh, oh, qblocks):
+        """one head: q/k/v/out [S, 1, D] bf16 for the whole sequence"""
+        qn = torchref.prologue(qh, wq, wl.eps, tab[:S])
+        kn = torchref.prologue(kh, wk, wl.eps, tab[:S])
+        ref = torchref.attend_blocks(qn, kn, vh, bl.row_ptr, bl.col_idx, qblocks, [0], scale)
+        mx, sm, n = 0.0, 0.0, 0
+        for (_, ib), r in ref.items():
+            d = (oh[ib * 128:ib * 128 + r.shape[0], 0].float() - r).abs()
+            mx, sm, n = max(mx, d.max().item()), sm + d.sum().item(), n + d.numel()
+        return mx, sm / max(n, 1)
+
+    qblocks = torchref.sample_blocks(nb, 6, seed=rank)
+    res = {"rank": rank, "query_blocks": qblocks, "heads": []}
+    mx_all, mean_all = 0.0, 0.0
+    if not seqm:
+        local = out.shape[1]
+        for j in sorted({0, local - 1}):
+            sl = slice(j, j + 1)
+            mx, mean = check(q[:, sl], k[:, sl], v[:, sl], out[:, sl], qblocks)
+            res["heads"].append(j)
+            mx_all, mean_all = max(mx_all, mx), max(mean_all, mean)
+    else:
+        for owner in range(ws):
+            hc = (owner * H) // ws  # the first head of the owner's exchanged share
+            parts = []
+            for t in (q, k, v, out):
+                x = t[:, hc:hc + 1].contiguous()
+                g = [torch.empty_like(x) for _ in range(ws)]
+                dist.all_gather(g, x)
+                parts.append(torch.cat(g)[:S])
+            if owner == rank:
+                mx, mean = check(*parts, qblocks)
+                res["heads"].append(hc)
+                mx_all, mean_all = max(mx_all, mx), max(mean_all, mean)
+    res["max_abs"], res["mean_abs"] = mx_all, mean_all
+    if ws > 1:
+        allr = [None] * ws
+        dist.all_gather_object(allr, res)
+    else:
+        allr = [res]
+    if rank != 0:
+        return None
+    worst_max = max(r["max_abs"] for r in allr)
+    worst_mean = max(r["mean_abs"] for r in allr)
+    return {"checker": "torch fp32 restatement (prologue + masked softmax over the kept blocks)",
+            "max_abs": worst_max, "mean_abs": worst_mean, "tolerance": list(PARITY_TOL),
+            "ok": worst_max <= PARITY_TOL[0] and worst_mean <= PARITY_TOL[1], "per_rank": allr}
 
 
 def run_ours(args):
@@ -242,7 +365,7 @@ def run_ours(args):
     def fill(shape, stream, mean=0.0, std=1.0):
         return rt.fill_normal(torch.empty(shape, dtype=bf, device=dev), wl.seed + rank, stream, mean, std)
 
-    mode = args.mode if ws > 1 else "replica"
+    mode = _mode(args, ws)
     # rows (tokens) and heads this rank holds
     if mode == "heads":
         h0, h1 = head_range(rank, ws, H)
@@ -310,6 +433,7 @@ def run_ours(args):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
     value = job_flops / (ms * 1e-3) / 1e12
+    parity = _parity(mode, ws, rank, wl, bl, q, k, v, out, wq, wk, tab, scale, dev)
     # our kernels per call: K prologue, Q prologue, attention; the C-ABI
     # sequence-sharded call adds, per head chunk, 3 packs and 1 unpack
     if mode == "seq":
@@ -383,20 +507,13 @@ def run_ours(args):
         peaks, src = _peaks()
         achieved = flops / (attn_ms * 1e-3) / 1e12
         traffic = TRAFFIC_BYTES.get(wl.name)
+        if traffic is not None:  # the capture's full-call figure, scaled to this rank's heads
+            traffic *= (H // ws if seqm else hl) / H
         line = {
             "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": ws, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": scaling,
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1) bf16; shapes of the workload)",
-            "config": {"workload": wl.name, "seq_len": S, "heads": H, "head_dim": 128, "block": 128,
-                       "density": round(bl.density, 4), "kept_blocks": bl.nnz, "flops_per_call": flops,
-                       "l2": "inputs larger than L2 (no flush)",
-                       "parallelism": {"replica": f"replicas x{ws} (weak)", "heads": f"head-sharded x{ws}",
-                                       "seq": f"sequence-sharded x{ws} (NCCL all-to-alls pipelined over head "
-                                               "chunks, C ABI)",
-                                       "seq_torch": f"sequence-sharded x{ws} (torch all_to_all_single)"}[mode],
-                       "prologue": (f"fused RMSNorm (eps {EPS:g}) + RoPE from the packed layout (rot 96, shared "
-                                    "inv_freq)" if wl.render else
-                                    f"fused RMSNorm (eps {EPS:g}) + RoPE (t/h/w 32/48/48, theta 1e4)")},
+            "config": _config(wl, bl, ws, mode),
             "e2e": {"value": job_flops / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": e2e_ms,
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
             "roofline": {"bound": "tensor", "kernel": "attn_tc_kernel", "achieved": achieved,
@@ -405,6 +522,7 @@ def run_ours(args):
                          "kernel_ms": attn_ms, "traffic": traffic},
             "gpu_launches": launches,
             "clocks": clk.summary(),
+            "parity": parity,
         }
         if ws == 1 and not args.no_cpu_baseline:
             cb = CpuBaseline(wl).sample(args.cpu_budget)
@@ -424,9 +542,9 @@ def main():
     ap.add_argument("--config", default="config2",
                     help="config1..config4, config5@<density> or production; default config2 (the 5 s 1344x768 clip)")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--mode", default="replica", choices=["replica", "heads", "seq", "seq_torch"],
-                    help="N>1 layout: independent full calls per rank (weak), heads split across ranks, or "
-                         "sequence-sharded with an all-to-all (strong)")
+    ap.add_argument("--mode", default=None, choices=["replica", "heads", "seq", "seq_torch"],
+                    help="N>1 layout: heads split across ranks (the default; strong), sequence-sharded with "
+                         "NCCL all-to-alls (strong), or independent full calls per rank (weak)")
     ap.add_argument("--cpu-budget", type=float, default=15.0, help="seconds of CPU baseline sampling")
     ap.add_argument("--ref-budget", type=float, default=120.0, help="total seconds for --impl reference")
     ap.add_argument("--no-cpu-baseline", action="store_true")

@@ -140,18 +140,21 @@ class BlockList:
         return self._dev[idx]
 
 
-def calibrate(spec: MaskSpec, target: float, radii_t=range(0, 16), n_random=range(0, 121, 2)) -> Tuple[MaskSpec, float]:
+def calibrate(spec: MaskSpec, target: float, radii_t=range(0, 16), n_random=range(0, 121, 2),
+              build=None) -> Tuple[MaskSpec, float]:
     """Choose (radius_t, n_random) whose token density is closest to target;
-    returns the spec and the measured density (reported, never assumed)."""
+    returns the spec and the measured density (reported, never assumed).
+    ``build`` (spec -> BlockList) defaults to the library's builder."""
+    build = build or BlockList.build
     best: Optional[Tuple[float, MaskSpec, float]] = None
     for rt in radii_t:
         base = replace(spec, radius_t=rt, n_random=0)
-        d0 = BlockList.build(base).density
+        d0 = build(base).density
         if d0 > target + 0.02 and best is not None:
             break
         for nr in n_random:
             cand = replace(base, n_random=nr)
-            d = BlockList.build(cand).density
+            d = build(cand).density
             err = abs(d - target)
             if best is None or err < best[0]:
                 best = (err, cand, d)

@@ -119,11 +119,12 @@ CONFIGS["production"] = Workload("production", heads=56, frames=37, height=15, w
                                  eps=1e-5, render=(332, 864, 480, 120))
 
 
-def config5(density: float) -> Workload:
-    """864x480 7 s clip, 40 heads; (radius_t, n_random) calibrated per density."""
+def config5(density: float, build=None) -> Workload:
+    """864x480 7 s clip, 40 heads; (radius_t, n_random) calibrated per density
+    (``build``: the block-list builder used for the calibration)."""
     from .blockmask import calibrate
 
     base = Workload(f"config5@{density:g}", heads=40, frames=43, height=30, width=54, radius_h=2,
                     radius_w=2, target_density=density)
-    spec, _ = calibrate(base.mask_spec(), density)
+    spec, _ = calibrate(base.mask_spec(), density, build=build)
     return replace(base, radius_t=spec.radius_t, n_random=spec.n_random)
