@@ -32,6 +32,9 @@
  *   h3c_blockmask_build   new: the compacted 128x128 block list (no reference
  *                         counterpart; prefix rule of AxialTopology.allows,
  *                         Sources/H3Attention/AxialTopology.swift:128-137)
+ *   h3c_blockmask_validate the refusal of a malformed mask, as
+ *                         AxialTopology.validate refuses mismatched geometry
+ *                         (Sources/H3Attention/AxialTopology.swift:67-70)
  *   h3c_device_info       H3Hardware Machine.detect (Sources/H3Hardware/
  *                         Machine.swift:48-56), for CUDA devices and NVLink
  *   h3c_init/h3c_destroy  the backend instance AttentionRegistry.resolve
@@ -141,6 +144,16 @@ h3c_status h3c_device_count(int* count);
  * NULL (query nnz first).  n_blocks = ceil(seq_len / block). */
 h3c_status h3c_blockmask_build(const h3c_mask_spec* spec, int32_t* row_ptr, int32_t* col_idx,
                                int64_t capacity, int64_t* nnz);
+/* Checks a caller's device block list before it is used: row_ptr[0] == 0,
+ * row_ptr non-decreasing with row_ptr[n_blocks] == nnz (no col_idx entry past
+ * nnz is read), every column in [0, n_blocks) and strictly ascending within
+ * its row.  The attention kernels trust the list (an unsorted or out-of-range
+ * list gives wrong output, not a fault, as TMA fills out-of-range tiles with
+ * zeros), so a caller that builds its own lists validates them once here.
+ * H3C_ERR_INVALID_ARGUMENT with the reasons in h3c_last_error otherwise.
+ * Synchronises `stream`. */
+h3c_status h3c_blockmask_validate(h3c_ctx* ctx, const int32_t* d_row_ptr, const int32_t* d_col_idx, int32_t n_blocks,
+                                  int64_t nnz, void* stream);
 /* Device builder, bit-identical to the host one.  d_row_ptr [n_blocks+1] and
  * d_col_idx [capacity] are device memory; *nnz is written on the host after a
  * stream synchronise.  Asynchronous otherwise. */
@@ -211,7 +224,12 @@ h3c_status h3c_prologue(h3c_ctx* ctx, h3c_view x, h3c_view out, int32_t seq_len,
 /* --- attention ------------------------------------------------------------ */
 /* Block-sparse attention forward, asynchronous on `stream` (a cudaStream_t,
  * NULL = legacy default stream).  With H3C_FUSE_PROLOGUE the context's
- * workspace holds the normalised keys (grown on demand with cudaMalloc). */
+ * workspace holds the normalised queries and keys (grown on demand with
+ * cudaMalloc; before a larger buffer replaces it the call waits for the last
+ * launch that read the old one, on whatever stream that ran).  A context
+ * serves one stream at a time: fused calls of one context on two streams
+ * without ordering between them race on its workspace and status word; use
+ * one context per concurrent stream. */
 h3c_status h3c_attn_fwd(h3c_ctx* ctx, const h3c_attn_args* args, void* stream);
 /* Bytes of workspace h3c_attn_fwd needs for these args. */
 h3c_status h3c_attn_workspace_size(const h3c_attn_args* args, size_t* bytes);
@@ -233,8 +251,16 @@ h3c_status h3c_attn_fwd_sync(h3c_ctx* ctx, const h3c_attn_args* args, void* stre
  * first call on a device resolves the array's address (make it before any
  * stream capture).  All calls share the array: calls that overlap on the GPU
  * race.  err (optional, err_len bytes) receives the message of a failure.
+ * A bounded device wait that gives up is recorded in a second fixed device
+ * word of the library, cleared at the start of every call: read it with
+ * h3c_attn_fwd_noalloc_status.
  * No counterpart in the reference: its MLX path has no allocation-free mode. */
 h3c_status h3c_attn_fwd_noalloc(const h3c_attn_args* args, void* stream, char* err, size_t err_len);
+/* Waits for the current device (cudaDeviceSynchronize), then reads and clears
+ * the status word of h3c_attn_fwd_noalloc: H3C_OK, or H3C_ERR_TIMEOUT when a
+ * bounded wait of the last call gave up (its output is invalid).  Allocates
+ * nothing.  No counterpart in the reference (see h3c_attn_fwd_noalloc). */
+h3c_status h3c_attn_fwd_noalloc_status(void);
 
 /* --- sequence-sharded path (NCCL) ------------------------------------------ */
 /* Multi-GPU layout for the longest sequences (one process per GPU).  The

@@ -1,6 +1,7 @@
 // The C ABI (include/h3cuda.h): argument checking, the context, the host
 // block-mask builder and dispatch to the kernels.  Every entry point returns
 // a status; nothing here aborts or exits.
+#include <climits>
 #include <cmath>
 #include <cstdlib>
 #include <cstring>
@@ -18,6 +19,8 @@ cudaError_t launch_mask_build(const h3c_mask_spec& sp, int32_t* counts, int32_t*
                               int64_t capacity, int64_t* d_nnz, cudaStream_t s);
 cudaError_t launch_fill_normal(uint16_t* out, int64_t n, uint64_t seed, uint64_t stream, double mean, double std,
                                int sm_count, cudaStream_t s);
+cudaError_t launch_validate_blocks(const int32_t* row_ptr, const int32_t* col_idx, int32_t n_blocks, int64_t nnz,
+                                   int32_t* flags, cudaStream_t s);
 }  // namespace h3
 
 namespace {
@@ -88,39 +91,52 @@ size_t workspace_bytes(const h3c_attn_args& a) {
 }
 
 h3c_status check_attn(h3c_ctx* ctx, const h3c_attn_args* a) {
-  if (!a) return fail(ctx, H3C_ERR_INVALID_ARGUMENT, "h3c_attn_fwd: null args");
-  if (a->head_dim != 128) return fail(ctx, H3C_ERR_UNSUPPORTED, "h3c_attn_fwd: head_dim must be 128");
-  if (a->block != 128) return fail(ctx, H3C_ERR_UNSUPPORTED, "h3c_attn_fwd: block must be 128");
+  std::string msg;
+  h3c_status st = h3::check_attn_args(a, "h3c_attn_fwd", &msg);
+  return st == H3C_OK ? st : fail(ctx, st, msg);
+}
+
+}  // namespace
+
+namespace h3 {
+
+h3c_status check_attn_args(const h3c_attn_args* a, const char* who, std::string* msg) {
+  auto bad = [&](h3c_status st, const char* why) {
+    *msg = std::string(who) + ": " + why;
+    return st;
+  };
+  if (!a) return bad(H3C_ERR_INVALID_ARGUMENT, "null args");
+  if (a->head_dim != 128) return bad(H3C_ERR_UNSUPPORTED, "head_dim must be 128");
+  if (a->block != 128) return bad(H3C_ERR_UNSUPPORTED, "block must be 128");
   if (a->seq_len <= 0 || a->heads <= 0 || a->head_count <= 0 || a->head_offset < 0 ||
       a->head_offset + a->head_count > a->heads)
-    return fail(ctx, H3C_ERR_INVALID_ARGUMENT, "h3c_attn_fwd: bad seq_len/heads/head range");
+    return bad(H3C_ERR_INVALID_ARGUMENT, "bad seq_len/heads/head range");
   if (!view_ok(a->q) || !view_ok(a->k) || !view_ok(a->v) || !view_ok(a->out))
-    return fail(ctx, H3C_ERR_INVALID_ARGUMENT, "h3c_attn_fwd: null pointer or non-positive stride in q/k/v/out");
-  if (!a->row_ptr || !a->col_idx) return fail(ctx, H3C_ERR_INVALID_ARGUMENT, "h3c_attn_fwd: null block list");
+    return bad(H3C_ERR_INVALID_ARGUMENT, "null pointer or non-positive stride in q/k/v/out");
+  if (!a->row_ptr || !a->col_idx) return bad(H3C_ERR_INVALID_ARGUMENT, "null block list");
   if (!(a->scale > 0.f) || !std::isfinite(a->scale))
-    return fail(ctx, H3C_ERR_INVALID_ARGUMENT, "h3c_attn_fwd: scale must be positive and finite");
+    return bad(H3C_ERR_INVALID_ARGUMENT, "scale must be positive and finite");
   if (a->flags & H3C_FUSE_PROLOGUE) {
     if (!a->q_norm_weight || !a->k_norm_weight)
-      return fail(ctx, H3C_ERR_INVALID_ARGUMENT, "h3c_attn_fwd: fused prologue needs q/k norm weights");
+      return bad(H3C_ERR_INVALID_ARGUMENT, "fused prologue needs q/k norm weights");
     if (!(a->flags & H3C_NO_ROPE)) {
-      if (!a->rope_table) return fail(ctx, H3C_ERR_INVALID_ARGUMENT, "h3c_attn_fwd: fused prologue needs a rope table");
-      if (a->rope_half <= 0 || 2 * a->rope_half > 128)
-        return fail(ctx, H3C_ERR_UNSUPPORTED, "h3c_attn_fwd: rope_half must be in [1, 64]");
+      if (!a->rope_table) return bad(H3C_ERR_INVALID_ARGUMENT, "fused prologue needs a rope table");
+      if (a->rope_half <= 0 || 2 * a->rope_half > 128) return bad(H3C_ERR_UNSUPPORTED, "rope_half must be in [1, 64]");
     }
-    if (!(a->eps >= 0.f)) return fail(ctx, H3C_ERR_INVALID_ARGUMENT, "h3c_attn_fwd: eps must be >= 0");
+    if (!(a->eps >= 0.f) || !std::isfinite(a->eps)) return bad(H3C_ERR_INVALID_ARGUMENT, "eps must be finite and >= 0");
     if (((uintptr_t)a->q_norm_weight & 15) || ((uintptr_t)a->k_norm_weight & 15) || ((uintptr_t)a->rope_table & 7))
-      return fail(ctx, H3C_ERR_UNSUPPORTED, "h3c_attn_fwd: norm weights need 16-byte, the rope table 8-byte alignment");
+      return bad(H3C_ERR_UNSUPPORTED, "norm weights need 16-byte, the rope table 8-byte alignment");
   }
   // 16-byte aligned rows are required by the vectorised and TMA loads.
   const h3c_view* vs[4] = {&a->q, &a->k, &a->v, &a->out};
   for (const h3c_view* v : vs) {
     if (((uintptr_t)v->ptr & 15) || (v->token_stride & 7) || (v->head_stride & 7))
-      return fail(ctx, H3C_ERR_UNSUPPORTED, "h3c_attn_fwd: operands need 16-byte aligned rows");
+      return bad(H3C_ERR_UNSUPPORTED, "operands need 16-byte aligned rows");
   }
   return H3C_OK;
 }
 
-}  // namespace
+}  // namespace h3
 
 extern "C" {
 
@@ -150,7 +166,9 @@ h3c_status h3c_init(int device, h3c_ctx** out) {
     delete ctx;
     return H3C_ERR_NO_DEVICE;
   }
-  if (cudaMalloc(&ctx->d_counter, 64) != cudaSuccess || cudaMemset(ctx->d_counter, 0, 64) != cudaSuccess) {
+  if (cudaMalloc(&ctx->d_counter, 64) != cudaSuccess || cudaMemset(ctx->d_counter, 0, 64) != cudaSuccess ||
+      cudaEventCreateWithFlags(&ctx->workspace_done, cudaEventDisableTiming) != cudaSuccess) {
+    if (ctx->d_counter) cudaFree(ctx->d_counter);
     delete ctx;
     return H3C_ERR_CUDA;
   }
@@ -162,7 +180,9 @@ h3c_status h3c_destroy(h3c_ctx* ctx) {
   if (!ctx) return H3C_ERR_INVALID_ARGUMENT;
   h3c_comm_destroy(ctx);
   cudaSetDevice(ctx->device);
+  if (ctx->workspace_done) cudaEventSynchronize(ctx->workspace_done);
   if (ctx->workspace) cudaFree(ctx->workspace);
+  if (ctx->workspace_done) cudaEventDestroy(ctx->workspace_done);
   if (ctx->d_counter) cudaFree(ctx->d_counter);
   delete ctx;
   return H3C_OK;
@@ -347,7 +367,9 @@ h3c_status h3c_attn_fwd(h3c_ctx* ctx, const h3c_attn_args* args, void* stream) {
     size_t need = workspace_bytes(a);
     if (ctx->workspace_bytes < need) {
       if (ctx->workspace) {
-        H3_CUDA_TRY(ctx, cudaStreamSynchronize(s));
+        // the last launch that read the old workspace may run on another
+        // stream: wait for it, then release the buffer
+        H3_CUDA_TRY(ctx, cudaEventSynchronize(ctx->workspace_done));
         cudaFree(ctx->workspace);
         ctx->workspace = nullptr;
         ctx->workspace_bytes = 0;
@@ -361,10 +383,10 @@ h3c_status h3c_attn_fwd(h3c_ctx* ctx, const h3c_attn_args* args, void* stream) {
     uint16_t* qn = kn + s_pad * (size_t)a.head_count * 128;
     const uint16_t* table = (a.flags & H3C_NO_ROPE) ? nullptr : (const uint16_t*)a.rope_table;
     const int half = table ? a.rope_half : 0;
-    H3_CUDA_TRY(ctx, h3::launch_prologue(L.k, L.k_tok, L.k_head, kn, (int64_t)a.head_count * 128, 128, a.seq_len,
-                                         a.head_count, (const uint16_t*)a.k_norm_weight, a.eps, table, half, s));
-    H3_CUDA_TRY(ctx, h3::launch_prologue(L.q, L.q_tok, L.q_head, qn, (int64_t)a.head_count * 128, 128, a.seq_len,
-                                         a.head_count, (const uint16_t*)a.q_norm_weight, a.eps, table, half, s));
+    H3_CUDA_TRY(ctx, h3::launch_prologue_qk(L.q, L.q_tok, L.q_head, qn, L.k, L.k_tok, L.k_head, kn,
+                                            (int64_t)a.head_count * 128, a.seq_len, a.head_count,
+                                            (const uint16_t*)a.q_norm_weight, (const uint16_t*)a.k_norm_weight,
+                                            a.eps, table, half, ctx->prop.multiProcessorCount, s));
     L.k = kn; L.k_tok = (int64_t)a.head_count * 128; L.k_head = 128;
     L.q = qn; L.q_tok = (int64_t)a.head_count * 128; L.q_head = 128;
   }
@@ -372,6 +394,7 @@ h3c_status h3c_attn_fwd(h3c_ctx* ctx, const h3c_attn_args* args, void* stream) {
   L.status = (int32_t*)(ctx->d_counter + 1);
   L.wait_limit_ns = 4000000000ull;
   L.drop_item = -1;
+  L.pdl = (a.flags & H3C_FUSE_PROLOGUE) ? 1 : 0;
   // Test hooks (fault injection on the host side): a K/V load the producer
   // skips, so that the consumers' bounded waits run out, and a shorter bound.
   if (const char* d = getenv("H3C_TEST_DROP_ITEM")) L.drop_item = atoi(d);
@@ -385,7 +408,29 @@ h3c_status h3c_attn_fwd(h3c_ctx* ctx, const h3c_attn_args* args, void* stream) {
     if (e != cudaSuccess) return fail(ctx, H3C_ERR_CUDA, "tcgen05 attention: " + why + cudaGetErrorString(e));
   }
   H3_CUDA_TRY(ctx, e);
+  if (a.flags & H3C_FUSE_PROLOGUE) H3_CUDA_TRY(ctx, cudaEventRecord(ctx->workspace_done, s));
   return H3C_OK;
+}
+
+h3c_status h3c_blockmask_validate(h3c_ctx* ctx, const int32_t* d_row_ptr, const int32_t* d_col_idx,
+                                  int32_t n_blocks, int64_t nnz, void* stream) {
+  if (!ctx) return H3C_ERR_INVALID_ARGUMENT;
+  if (!d_row_ptr || (!d_col_idx && nnz > 0) || n_blocks <= 0 || nnz < 0 || nnz > INT32_MAX)
+    return fail(ctx, H3C_ERR_INVALID_ARGUMENT, "h3c_blockmask_validate: invalid argument");
+  cudaStream_t s = (cudaStream_t)stream;
+  H3_CUDA_TRY(ctx, cudaSetDevice(ctx->device));
+  int32_t* flags = (int32_t*)(ctx->d_counter + 2);
+  H3_CUDA_TRY(ctx, h3::launch_validate_blocks(d_row_ptr, d_col_idx, n_blocks, nnz, flags, s));
+  int32_t bad = 0;
+  H3_CUDA_TRY(ctx, cudaMemcpyAsync(&bad, flags, sizeof(bad), cudaMemcpyDeviceToHost, s));
+  H3_CUDA_TRY(ctx, cudaStreamSynchronize(s));
+  if (!bad) return H3C_OK;
+  std::string why = "h3c_blockmask_validate:";
+  if (bad & 1) why += " row_ptr[0] != 0 or row_ptr[n_blocks] != nnz;";
+  if (bad & 2) why += " row_ptr decreasing or outside [0, nnz];";
+  if (bad & 4) why += " a column index outside [0, n_blocks);";
+  if (bad & 8) why += " columns of a row not strictly ascending;";
+  return fail(ctx, H3C_ERR_INVALID_ARGUMENT, why);
 }
 
 h3c_status h3c_attn_fwd_sync(h3c_ctx* ctx, const h3c_attn_args* args, void* stream) {

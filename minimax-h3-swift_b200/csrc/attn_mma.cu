@@ -10,6 +10,8 @@
 // value tiles of 64 keys are double-buffered in shared memory with cp.async;
 // shared rows are 256 B with the 16-byte chunk index XOR-swizzled by (row & 7)
 // so that ldmatrix reads are bank-conflict free.
+#include <mutex>
+
 #include "common.cuh"
 
 namespace h3 {
@@ -226,17 +228,18 @@ __global__ void __launch_bounds__(kThreads, 1) attn_mma_kernel(AttnLaunch a) {
 
 cudaError_t launch_attn_mma(const AttnLaunch& a, cudaStream_t s) {
   const int smem = kRows * 256 + 4 * kTileKeys * 256;
-  // function attributes are per device context: remember them per device
-  static bool attr_set[64] = {};
+  // function attributes are per device context: set them once per device
+  // (std::call_once: concurrent first calls from several host threads are safe)
+  static std::once_flag once[64];
+  static cudaError_t set_result[64];
   int dev = 0;
   cudaError_t de = cudaGetDevice(&dev);
   if (de != cudaSuccess) return de;
   if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
-  if (!attr_set[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(attn_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    if (e != cudaSuccess) return e;
-    attr_set[dev] = true;
-  }
+  std::call_once(once[dev], [dev, smem] {
+    set_result[dev] = cudaFuncSetAttribute(attn_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  });
+  if (set_result[dev] != cudaSuccess) return set_result[dev];
   dim3 grid(a.n_blocks, a.head_count);
   attn_mma_kernel<<<grid, kThreads, smem, s>>>(a);
   return cudaGetLastError();

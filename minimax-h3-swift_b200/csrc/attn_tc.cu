@@ -33,6 +33,7 @@
 #include <cuda.h>
 
 #include <climits>
+#include <mutex>
 #include <cstdlib>
 #include <type_traits>
 
@@ -311,6 +312,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       // Walks the union of the two tiles' ascending block lists; every key
       // block in the union is loaded once (K then V) and serves both tiles.
       if (lane == 0) {
+        // q and k may be the output of the prologue kernel this grid was
+        // launched as a dependent of: wait for it before the first load
+        if (a.pdl) asm volatile("griddepcontrol.wait;" ::: "memory");
         for (int t = 0; t < ntile; ++t) {
           uint32_t bar = smem_u32(&bars->q_full[t]);
           mbar_expect_tx(bar, kTileBytes);
@@ -622,15 +626,16 @@ typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t,
                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 
+// Looked up once per process (thread-safe static initialisation).
 EncodeTiledFn get_encode() {
-  static EncodeTiledFn fn = nullptr;
-  if (!fn) {
+  static const EncodeTiledFn fn = [] {
     void* p = nullptr;
     cudaDriverEntryPointQueryResult q;
     if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
         q == cudaDriverEntryPointSuccess)
-      fn = (EncodeTiledFn)p;
-  }
+      return (EncodeTiledFn)p;
+    return (EncodeTiledFn) nullptr;
+  }();
   return fn;
 }
 
@@ -661,26 +666,39 @@ constexpr int kDefaultEmu = 0;
 template <int EMU>
 cudaError_t launch_variant(dim3 grid, cudaStream_t s, const CUtensorMap& mq, const CUtensorMap& mk,
                            const CUtensorMap& mv, const AttnLaunch& a) {
-  // function attributes are per device context: remember them per device
-  static bool attr_set[64] = {};  // one table per template instance
+  // function attributes are per device context: set them once per device
+  // (std::call_once: host threads making their first call together are safe)
+  static std::once_flag once[64];  // one table per template instance
+  static cudaError_t set_result[64];
   int dev = 0;
   cudaError_t de = cudaGetDevice(&dev);
   if (de != cudaSuccess) return de;
   if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
-  if (!attr_set[dev]) {
+  std::call_once(once[dev], [dev] {
     cudaError_t e =
         cudaFuncSetAttribute(attn_tc_kernel<EMU>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
-    if (e != cudaSuccess) return e;
     // setmaxnreg draws on the registers the block was launched with; the
     // kernel's split needs exactly 168 per thread at launch.
     cudaFuncAttributes fa;
-    e = cudaFuncGetAttributes(&fa, attn_tc_kernel<EMU>);
-    if (e != cudaSuccess) return e;
-    if (fa.numRegs != 168) return cudaErrorInvalidConfiguration;
-    attr_set[dev] = true;
-  }
-  attn_tc_kernel<EMU><<<grid, kThreads, kSmemBytes, s>>>(mq, mk, mv, a);
-  return cudaGetLastError();
+    if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, attn_tc_kernel<EMU>);
+    if (e == cudaSuccess && fa.numRegs != 168) e = cudaErrorInvalidConfiguration;
+    set_result[dev] = e;
+  });
+  if (set_result[dev] != cudaSuccess) return set_result[dev];
+  // Programmatic dependent launch after the prologue: the CTAs are placed as
+  // the prologue's retire and do their set-up (barriers, TMEM) while its
+  // tail runs; the producer waits for the prologue before loading Q and K.
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = kSmemBytes;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = a.pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, attn_tc_kernel<EMU>, mq, mk, mv, a);
 }
 
 }  // namespace
@@ -693,12 +711,11 @@ cudaError_t launch_attn_tc(const AttnLaunch& a, cudaStream_t s, std::string* err
     return cudaErrorInvalidValue;
   // Share of exponentials computed on the FMA pipe, in eighths (tuning knob
   // H3C_EXP_EMU, read once; default chosen by measurement).
-  static int emu = -1;
-  if (emu < 0) {
+  static const int emu = [] {
     const char* env = getenv("H3C_EXP_EMU");
-    emu = env ? atoi(env) : kDefaultEmu;
-    if (emu < 0 || emu > 8) emu = kDefaultEmu;
-  }
+    const int v = env ? atoi(env) : kDefaultEmu;
+    return (v < 0 || v > 8) ? kDefaultEmu : v;
+  }();
   dim3 grid((a.n_blocks + 1) / 2, a.head_count);
   switch (emu) {
     case 0: return launch_variant<0>(grid, s, mq, mk, mv, a);

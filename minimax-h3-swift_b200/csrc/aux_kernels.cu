@@ -159,6 +159,134 @@ __global__ void __launch_bounds__(256) prologue_pairs_kernel(const uint16_t* __r
       make_uint2(*reinterpret_cast<uint32_t*>(&B[0]), *reinterpret_cast<uint32_t*>(&B[1]));
 }
 
+// Both operands of the fused call in one launch.  A warp owns one operand
+// (its norm weights stay in registers) and walks tokens; for each token it
+// loads the token's RoPE table entries once into registers and then
+// normalises and rotates every head of that token, four rows at a time
+// (8 threads per 128-channel row, two 16-byte loads and stores per thread,
+// two heads in flight per thread).  Thread t of a row owns the rotation
+// pairs 8t..8t+7 (channels 8t.. and half+8t..) when 8t < half, else 16
+// contiguous pass-through channels from 2*half up; half must be a multiple
+// of 8 (64 for the benchmark, 48 for the production model) and the table
+// 16-byte aligned.  Arithmetic as prologue_pairs_kernel.
+struct ProOperand {
+  const uint16_t* x;
+  int64_t x_tok, x_head;
+  uint16_t* y;
+  int64_t y_tok, y_head;
+  const uint16_t* w;
+};
+
+__device__ __forceinline__ void unpack8(uint4 u, float* f) {
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    f[2 * i] = __uint_as_float(w[i] << 16);
+    f[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+  }
+}
+
+__device__ __forceinline__ uint32_t pack2(float lo, float hi) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
+template <int U>
+__global__ void __launch_bounds__(256, 3) prologue_qk_kernel(ProOperand op0, ProOperand op1, int32_t seq_len,
+                                                             int32_t head_count, float eps,
+                                                             const uint16_t* __restrict__ table, int32_t half) {
+  // PDL: the dependent attention kernel may be scheduled as SMs free up; it
+  // waits for this grid's completion before it reads the normalised rows
+  asm volatile("griddepcontrol.launch_dependents;");
+  const int lane = threadIdx.x & 31, grp = lane >> 3, t = lane & 7;
+  const int64_t gw = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nw = ((int64_t)gridDim.x * blockDim.x) >> 5;  // even: 8 warps per CTA
+  // field by field: a reference to either parameter would put both in local memory
+  const bool second = gw & 1;
+  const uint16_t* __restrict__ px = second ? op1.x : op0.x;
+  uint16_t* __restrict__ py = second ? op1.y : op0.y;
+  const int64_t x_tok = second ? op1.x_tok : op0.x_tok, x_head = second ? op1.x_head : op0.x_head;
+  const int64_t y_tok = second ? op1.y_tok : op0.y_tok, y_head = second ? op1.y_head : op0.y_head;
+  const uint16_t* pw = second ? op1.w : op0.w;
+  const bool rot = table != nullptr && 8 * t < half;
+  const int hh = table ? half : 0;
+  const int ca = rot ? 8 * t : 2 * hh + 16 * (t - hh / 8);
+  const int cb = rot ? half + 8 * t : ca + 8;
+  const uint4 wpa = *reinterpret_cast<const uint4*>(pw + ca), wpb = *reinterpret_cast<const uint4*>(pw + cb);
+
+  for (int64_t s = gw >> 1; s < seq_len; s += nw >> 1) {
+    // the token's rotation entries (c, -s, s, c) for pairs 8t..8t+7; read
+    // per row (L1 hits after the token's first head)
+    const uint4* tp = rot ? reinterpret_cast<const uint4*>(table + (s * half + 8 * t) * 4) : nullptr;
+    const uint16_t* xs = px + s * x_tok;
+    uint16_t* ys = py + s * y_tok;
+    for (int h0 = grp; h0 < head_count; h0 += 4 * U) {
+      // U heads per thread in flight: h0, h0 + 4, ...
+      uint4 ra[U], rb[U];
+      bool live[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int h = h0 + 4 * u;
+        live[u] = h < head_count;
+        if (live[u]) {
+          const uint16_t* xr = xs + h * x_head;
+          ra[u] = __ldcs(reinterpret_cast<const uint4*>(xr + ca));
+          rb[u] = __ldcs(reinterpret_cast<const uint4*>(xr + cb));
+        } else {
+          ra[u] = rb[u] = make_uint4(0, 0, 0, 0);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        float a[8], b[8];
+        unpack8(ra[u], a);
+        unpack8(rb[u], b);
+        float ss = 0.f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) ss += a[i] * a[i] + b[i] * b[i];
+        ss += __shfl_xor_sync(0xffffffff, ss, 4);
+        ss += __shfl_xor_sync(0xffffffff, ss, 2);
+        ss += __shfl_xor_sync(0xffffffff, ss, 1);
+        if (!live[u]) continue;
+        const float inv = 1.0f / sqrtf(ss / 128.f + eps);
+        float wa[8], wb[8];
+        unpack8(wpa, wa);
+        unpack8(wpb, wb);
+        uint32_t A[4], B[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          A[k] = pack2((a[2 * k] * inv) * wa[2 * k], (a[2 * k + 1] * inv) * wa[2 * k + 1]);
+          B[k] = pack2((b[2 * k] * inv) * wb[2 * k], (b[2 * k + 1] * inv) * wb[2 * k + 1]);
+        }
+        if (rot) {
+          // each product and each sum rounded to bf16 once (see
+          // prologue_pairs_kernel for why the packed bf16 ops are exact);
+          // tp[k] holds the entries of pairs 8t+2k and 8t+2k+1
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const uint4 ek = tp[k];
+            const uint32_t cw = __byte_perm(ek.x, ek.z, 0x5410), nsw = __byte_perm(ek.x, ek.z, 0x7632);
+            const uint32_t sw = __byte_perm(ek.y, ek.w, 0x5410), c2w = __byte_perm(ek.y, ek.w, 0x7632);
+            const __nv_bfloat162 c = *reinterpret_cast<const __nv_bfloat162*>(&cw);
+            const __nv_bfloat162 ns = *reinterpret_cast<const __nv_bfloat162*>(&nsw);
+            const __nv_bfloat162 sn = *reinterpret_cast<const __nv_bfloat162*>(&sw);
+            const __nv_bfloat162 c2 = *reinterpret_cast<const __nv_bfloat162*>(&c2w);
+            const __nv_bfloat162 av = *reinterpret_cast<const __nv_bfloat162*>(&A[k]);
+            const __nv_bfloat162 bv = *reinterpret_cast<const __nv_bfloat162*>(&B[k]);
+            const __nv_bfloat162 r0 = __hadd2_rn(__hmul2_rn(c, av), __hmul2_rn(ns, bv));
+            const __nv_bfloat162 r1 = __hadd2_rn(__hmul2_rn(sn, av), __hmul2_rn(c2, bv));
+            A[k] = *reinterpret_cast<const uint32_t*>(&r0);
+            B[k] = *reinterpret_cast<const uint32_t*>(&r1);
+          }
+        }
+        uint16_t* yr = ys + (h0 + 4 * u) * y_head;
+        *reinterpret_cast<uint4*>(yr + ca) = make_uint4(A[0], A[1], A[2], A[3]);
+        *reinterpret_cast<uint4*>(yr + cb) = make_uint4(B[0], B[1], B[2], B[3]);
+      }
+    }
+  }
+}
+
 // -------------------------------------------------------------- rope table
 // Follows H3RoPE.angles / rotationTable (Sources/H3Modules/H3Transformer.swift:62-78):
 // fp32 inv_freq, fp32 angle = pos * inv, cos/sin evaluated in double on the
@@ -327,6 +455,32 @@ __global__ void fill_normal_kernel(uint16_t* __restrict__ out, int64_t n, uint64
   }
 }
 
+
+// ------------------------------------------------------ block-list validation
+// One thread per query block: row_ptr[0] == 0, row_ptr non-decreasing and
+// within [0, nnz] (so no col_idx entry past the caller's nnz is ever read),
+// every col_idx of the row in [0, n_blocks) and strictly ascending.
+// Violations are OR-ed into *flags (1: row_ptr[0] != 0 or row_ptr[n_blocks]
+// != nnz, 2: row_ptr decreasing or outside [0, nnz], 4: column out of range,
+// 8: columns not strictly ascending).
+__global__ void validate_blocks_kernel(const int32_t* __restrict__ row_ptr, const int32_t* __restrict__ col_idx,
+                                       int32_t n_blocks, int64_t nnz, int32_t* flags) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n_blocks) return;
+  int bad = 0;
+  if (i == 0 && row_ptr[0] != 0) bad |= 1;
+  if (i == n_blocks - 1 && (int64_t)row_ptr[n_blocks] != nnz) bad |= 1;
+  const int p0 = row_ptr[i], p1 = row_ptr[i + 1];
+  if (p1 < p0 || p0 < 0 || (int64_t)p1 > nnz) bad |= 2;
+  int prev = -1;
+  for (int p = p0; p < p1 && !(bad & 2); ++p) {
+    const int c = col_idx[p];
+    if (c < 0 || c >= n_blocks) bad |= 4;
+    if (c <= prev) bad |= 8;
+    prev = c;
+  }
+  if (bad) atomicOr(flags, bad);
+}
 }  // namespace
 
 cudaError_t launch_prologue(const uint16_t* x, int64_t x_tok, int64_t x_head, uint16_t* y, int64_t y_tok,
@@ -343,6 +497,34 @@ cudaError_t launch_prologue(const uint16_t* x, int64_t x_tok, int64_t x_head, ui
   }
   prologue_kernel<<<(unsigned)((rows + 15) / 16), 256, 0, s>>>(x, x_tok, x_head, y, y_tok, y_head, seq_len,
                                                              head_count, w, eps, table, half);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_prologue_qk(const uint16_t* q, int64_t q_tok, int64_t q_head, uint16_t* qn, const uint16_t* k,
+                               int64_t k_tok, int64_t k_head, uint16_t* kn, int64_t n_tok, int32_t seq_len,
+                               int32_t head_count, const uint16_t* wq, const uint16_t* wk, float eps,
+                               const uint16_t* table, int32_t half, int sm_count, cudaStream_t s) {
+  if ((int64_t)seq_len * head_count == 0) return cudaSuccess;
+  const bool fast = (table == nullptr || (half % 8 == 0 && ((uintptr_t)table & 15) == 0)) &&
+                    !((uintptr_t)wq & 15) && !((uintptr_t)wk & 15);
+  if (!fast) {  // any other half: the per-operand kernels
+    cudaError_t e = launch_prologue(k, k_tok, k_head, kn, n_tok, 128, seq_len, head_count, wk, eps, table, half, s);
+    if (e != cudaSuccess) return e;
+    return launch_prologue(q, q_tok, q_head, qn, n_tok, 128, seq_len, head_count, wq, eps, table, half, s);
+  }
+  ProOperand o0{k, k_tok, k_head, kn, n_tok, 128, wk};
+  ProOperand o1{q, q_tok, q_head, qn, n_tok, 128, wq};
+  // 8 warps per CTA, two operands: enough warps for every SM, at most one
+  // token per warp
+  int64_t want = ((int64_t)seq_len * 2 + 7) / 8;
+  // two heads in flight per thread (measured best of 1-4 at config 2:
+  // 0.88 ms for 5.12 GB, 0.89 of the copy bandwidth), three 256-thread CTAs
+  // resident per SM at 80 registers
+  constexpr int kHeadsInFlight = 2;
+  int64_t cap = (int64_t)sm_count * 3;
+  const unsigned grid = (unsigned)(want < cap ? want : cap);
+  prologue_qk_kernel<kHeadsInFlight><<<grid, 256, 0, s>>>(o0, o1, seq_len, head_count, eps, table,
+                                                            table ? half : 0);
   return cudaGetLastError();
 }
 
@@ -381,6 +563,14 @@ cudaError_t launch_mask_build(const h3c_mask_spec& sp, int32_t* counts, int32_t*
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   mask_rows_kernel<<<m.nb, 256, smem, s>>>(m, nullptr, row_ptr, col_idx, capacity, 1);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_validate_blocks(const int32_t* row_ptr, const int32_t* col_idx, int32_t n_blocks, int64_t nnz,
+                                   int32_t* flags, cudaStream_t s) {
+  cudaError_t e = cudaMemsetAsync(flags, 0, sizeof(int32_t), s);
+  if (e != cudaSuccess) return e;
+  validate_blocks_kernel<<<(n_blocks + 255) / 256, 256, 0, s>>>(row_ptr, col_idx, n_blocks, nnz, flags);
   return cudaGetLastError();
 }
 

@@ -27,8 +27,13 @@
 //    threads, without ordering between them) race on it.  Nothing in it has
 //    to start at zero: every row a call reads is written by that call first
 //    (padding rows past seq_len are never read; TMA fills them with zeros).
+//  * A bounded device wait that gives up (H3C_ERR_TIMEOUT: the output of that
+//    call is invalid) is recorded in a second file-scope device word,
+//    g_noalloc_status, cleared at the start of every call;
+//    h3c_attn_fwd_noalloc_status() reads and clears it.
 //  * No cudaMalloc, cudaFree or allocating library routine is called.
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 
@@ -40,20 +45,35 @@ constexpr size_t kNoAllocScratchBytes = 32ull << 20;
 constexpr int kMaxDevices = 64;
 
 __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
+__device__ __align__(16) int32_t g_noalloc_status;
 
 std::mutex g_mu;
 void* g_scratch_addr[kMaxDevices] = {};
+int32_t* g_status_addr[kMaxDevices] = {};
+
+// Device addresses of the scratch array and the status word on the current
+// device, looked up once per device with that device current.
+cudaError_t resolve(int dev, void** scratch, int32_t** status) {
+  std::lock_guard<std::mutex> lock(g_mu);
+  if (!g_scratch_addr[dev] || !g_status_addr[dev]) {
+    void* a = nullptr;
+    void* b = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&a, g_noalloc_scratch);
+    if (e == cudaSuccess) e = cudaGetSymbolAddress(&b, g_noalloc_status);
+    if (e != cudaSuccess) return e;
+    g_scratch_addr[dev] = a;
+    g_status_addr[dev] = (int32_t*)b;
+  }
+  *scratch = g_scratch_addr[dev];
+  *status = g_status_addr[dev];
+  return cudaSuccess;
+}
 
 h3c_status report(char* err, size_t err_len, h3c_status st, const char* msg) {
   if (err && err_len) {
     std::snprintf(err, err_len, "%s", msg);
   }
   return st;
-}
-
-bool view_aligned(const h3c_view& v) {
-  return v.ptr && v.token_stride > 0 && v.head_stride > 0 && !((uintptr_t)v.ptr & 15) && !(v.token_stride & 7) &&
-         !(v.head_stride & 7);
 }
 
 }  // namespace
@@ -67,21 +87,12 @@ extern "C" h3c_status h3c_attn_fwd_noalloc(const h3c_attn_args* args, void* stre
                   "h3c_attn_fwd_noalloc: only the fused path (H3C_FUSE_PROLOGUE) uses scratch; call h3c_attn_fwd");
   if (a.flags & H3C_KERNEL_MMA_SYNC)
     return report(err, err_len, H3C_ERR_UNSUPPORTED, "h3c_attn_fwd_noalloc: tcgen05 kernel only");
-  if (a.head_dim != 128 || a.block != 128)
-    return report(err, err_len, H3C_ERR_UNSUPPORTED, "h3c_attn_fwd_noalloc: head_dim and block must be 128");
-  if (a.seq_len <= 0 || a.heads <= 0 || a.head_count <= 0 || a.head_offset < 0 || a.head_offset + a.head_count > a.heads)
-    return report(err, err_len, H3C_ERR_INVALID_ARGUMENT, "h3c_attn_fwd_noalloc: bad seq_len/heads/head range");
-  if (!view_aligned(a.q) || !view_aligned(a.k) || !view_aligned(a.v) || !view_aligned(a.out))
-    return report(err, err_len, H3C_ERR_INVALID_ARGUMENT,
-                  "h3c_attn_fwd_noalloc: q/k/v/out need non-null, 16-byte aligned rows");
-  if (!a.row_ptr || !a.col_idx || !a.q_norm_weight || !a.k_norm_weight || !(a.scale > 0.f) || !(a.eps >= 0.f))
-    return report(err, err_len, H3C_ERR_INVALID_ARGUMENT,
-                  "h3c_attn_fwd_noalloc: null block list or norm weight, or bad scale/eps");
+  {
+    std::string msg;
+    h3c_status st = h3::check_attn_args(args, "h3c_attn_fwd_noalloc", &msg);
+    if (st != H3C_OK) return report(err, err_len, st, msg.c_str());
+  }
   const bool rope = !(a.flags & H3C_NO_ROPE);
-  if (rope && (!a.rope_table || a.rope_half <= 0 || 2 * a.rope_half > 128))
-    return report(err, err_len, H3C_ERR_INVALID_ARGUMENT, "h3c_attn_fwd_noalloc: rope table / rope_half invalid");
-  if (((uintptr_t)a.q_norm_weight & 15) || ((uintptr_t)a.k_norm_weight & 15) || ((uintptr_t)a.rope_table & 7))
-    return report(err, err_len, H3C_ERR_UNSUPPORTED, "h3c_attn_fwd_noalloc: misaligned norm weight or rope table");
 
   const int n_blocks = (a.seq_len + 127) / 128;
   const size_t rows = (size_t)n_blocks * 128 * (size_t)a.head_count;
@@ -99,17 +110,10 @@ extern "C" h3c_status h3c_attn_fwd_noalloc(const h3c_attn_args* args, void* stre
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices)
     return report(err, err_len, H3C_ERR_NO_DEVICE, "h3c_attn_fwd_noalloc: no usable current device");
   void* scratch = nullptr;
+  int32_t* status = nullptr;
   {
-    std::lock_guard<std::mutex> lock(g_mu);
-    if (!g_scratch_addr[dev]) {
-      // once per device, with that device current
-      cudaError_t e = cudaGetSymbolAddress(&g_scratch_addr[dev], g_noalloc_scratch);
-      if (e != cudaSuccess) {
-        g_scratch_addr[dev] = nullptr;
-        return report(err, err_len, H3C_ERR_CUDA, cudaGetErrorString(e));
-      }
-    }
-    scratch = g_scratch_addr[dev];
+    cudaError_t e = resolve(dev, &scratch, &status);
+    if (e != cudaSuccess) return report(err, err_len, H3C_ERR_CUDA, cudaGetErrorString(e));
   }
 
   cudaStream_t s = (cudaStream_t)stream;
@@ -122,11 +126,13 @@ extern "C" h3c_status h3c_attn_fwd_noalloc(const h3c_attn_args* args, void* stre
   const uint16_t* table = rope ? (const uint16_t*)a.rope_table : nullptr;
   const int half = rope ? a.rope_half : 0;
   const int64_t ntok = (int64_t)a.head_count * 128;
-  cudaError_t e = h3::launch_prologue(k, a.k.token_stride, a.k.head_stride, kn, ntok, 128, a.seq_len, a.head_count,
-                                      (const uint16_t*)a.k_norm_weight, a.eps, table, half, s);
+  cudaError_t e = cudaMemsetAsync(status, 0, sizeof(int32_t), s);
+  int sms = 148;
+  if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   if (e == cudaSuccess)
-    e = h3::launch_prologue(q, a.q.token_stride, a.q.head_stride, qn, ntok, 128, a.seq_len, a.head_count,
-                            (const uint16_t*)a.q_norm_weight, a.eps, table, half, s);
+    e = h3::launch_prologue_qk(q, a.q.token_stride, a.q.head_stride, qn, k, a.k.token_stride, a.k.head_stride, kn,
+                               ntok, a.seq_len, a.head_count, (const uint16_t*)a.q_norm_weight,
+                               (const uint16_t*)a.k_norm_weight, a.eps, table, half, sms, s);
   if (e != cudaSuccess) return report(err, err_len, H3C_ERR_CUDA, cudaGetErrorString(e));
   L.q = qn; L.q_tok = ntok; L.q_head = 128;
   L.k = kn; L.k_tok = ntok; L.k_head = 128;
@@ -138,9 +144,13 @@ extern "C" h3c_status h3c_attn_fwd_noalloc(const h3c_attn_args* args, void* stre
   L.scale_log2 = a.scale * 1.4426950408889634f;
   L.row_ptr = a.row_ptr;
   L.col_idx = a.col_idx;
-  L.status = nullptr;
+  L.status = status;
   L.wait_limit_ns = 4000000000ull;
   L.drop_item = -1;
+  L.pdl = (a.flags & H3C_FUSE_PROLOGUE) ? 1 : 0;
+  // the same host-side fault-injection hooks as h3c_attn_fwd (tests only)
+  if (const char* d = getenv("H3C_TEST_DROP_ITEM")) L.drop_item = atoi(d);
+  if (const char* w = getenv("H3C_TEST_WAIT_LIMIT_NS")) L.wait_limit_ns = strtoull(w, nullptr, 10);
   std::string why;
   e = h3::launch_attn_tc(L, s, &why);
   if (e != cudaSuccess) {
@@ -148,4 +158,18 @@ extern "C" h3c_status h3c_attn_fwd_noalloc(const h3c_attn_args* args, void* stre
     return report(err, err_len, H3C_ERR_CUDA, why.c_str());
   }
   return H3C_OK;
+}
+
+extern "C" h3c_status h3c_attn_fwd_noalloc_status(void) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return H3C_ERR_NO_DEVICE;
+  void* scratch = nullptr;
+  int32_t* status = nullptr;
+  if (resolve(dev, &scratch, &status) != cudaSuccess) return H3C_ERR_CUDA;
+  int32_t word = 0;
+  if (cudaDeviceSynchronize() != cudaSuccess ||
+      cudaMemcpy(&word, status, sizeof(word), cudaMemcpyDeviceToHost) != cudaSuccess ||
+      cudaMemset(status, 0, sizeof(int32_t)) != cudaSuccess)
+    return H3C_ERR_CUDA;
+  return (h3c_status)word;
 }

@@ -210,7 +210,9 @@ h3c_status h3c_attn_fwd_seqshard(h3c_ctx* ctx, const h3c_attn_args* args, void* 
   const size_t need = 5 * elems * sizeof(uint16_t);  // send buffer + exchanged q, k, v and the output
   if (st->buf_bytes < need) {
     if (st->buf) {
-      H3_CUDA_TRY(ctx, cudaStreamSynchronize(s));
+      // the previous call (on any stream) ends with out_done on the side
+      // stream, after every launch that used the buffer
+      H3_CUDA_TRY(ctx, cudaEventSynchronize(st->out_done));
       H3_CUDA_TRY(ctx, cudaStreamSynchronize(st->side));
       cudaFree(st->buf);
       st->buf = nullptr;
@@ -232,12 +234,13 @@ h3c_status h3c_attn_fwd_seqshard(h3c_ctx* ctx, const h3c_attn_args* args, void* 
   // Pipeline over head chunks: the exchange of chunk c+1 (side stream)
   // overlaps the attention of chunk c (caller's stream), and the output of
   // chunk c travels back while chunk c+1 computes.
-  static int chunks_env = -1;  // H3C_SEQ_CHUNKS: head chunks of the pipeline (tuning knob)
-  if (chunks_env < 0) {
+  // H3C_SEQ_CHUNKS: head chunks of the pipeline (tuning knob), read once
+  // (thread-safe static initialisation)
+  static const int chunks_env = [] {
     const char* e = getenv("H3C_SEQ_CHUNKS");
-    chunks_env = e ? atoi(e) : kDefaultChunks;
-    if (chunks_env < 1 || chunks_env > kMaxChunks) chunks_env = kDefaultChunks;
-  }
+    const int c = e ? atoi(e) : kDefaultChunks;
+    return (c < 1 || c > kMaxChunks) ? kDefaultChunks : c;
+  }();
   const int nchunk = hp < chunks_env ? hp : chunks_env;
   cudaStream_t x = st->side;
 

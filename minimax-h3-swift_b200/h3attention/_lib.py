@@ -39,6 +39,7 @@ EXPORTS = (
     "h3c_prologue", "h3c_attn_fwd", "h3c_attn_workspace_size", "h3c_attn_fwd_sync",
     "h3c_fill_normal_bf16", "h3c_attn_fwd_noalloc", "h3c_device_status",
     "h3c_comm_unique_id", "h3c_comm_init", "h3c_comm_destroy", "h3c_attn_fwd_seqshard",
+    "h3c_blockmask_validate", "h3c_attn_fwd_noalloc_status",
 )
 
 
@@ -147,6 +148,8 @@ def load() -> C.CDLL:
             "h3c_comm_destroy": ([vp], st),
             "h3c_attn_fwd_seqshard": ([vp, C.POINTER(AttnArgs), vp], st),
             "h3c_attn_fwd_noalloc": ([C.POINTER(AttnArgs), vp, C.c_char_p, C.c_size_t], st),
+            "h3c_attn_fwd_noalloc_status": ([], st),
+            "h3c_blockmask_validate": ([vp, vp, vp, i32, i64, vp], st),
         }
         for name, (args, res) in sig.items():
             fn = getattr(L, name)

@@ -176,6 +176,16 @@ class Runtime:
                                                 _stream_ptr(stream)))
         return out
 
+    def validate_blocks(self, blocks, stream=None):
+        """Check a device block list (row_ptr [n_blocks+1], col_idx [nnz]
+        int32 tensors on this device): row_ptr starts at 0, never decreases
+        and ends at nnz; columns in [0, n_blocks), strictly ascending per
+        row.  Raises H3CError(H3C_ERR_INVALID_ARGUMENT) with the reason.
+        Synchronises the stream."""
+        rp, ci = blocks
+        self._check(self.L.h3c_blockmask_validate(self.ctx, rp.data_ptr(), ci.data_ptr(), rp.numel() - 1, ci.numel(),
+                                                  _stream_ptr(stream)))
+
     def blockmask_device(self, spec, capacity: int, stream=None):
         import torch
 
