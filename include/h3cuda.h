@@ -37,6 +37,8 @@
  *                         (Sources/H3Attention/AxialTopology.swift:67-70)
  *   h3c_device_info       H3Hardware Machine.detect (Sources/H3Hardware/
  *                         Machine.swift:48-56), for CUDA devices and NVLink
+ *   h3c_nvlink_query      the NVLink / NVSwitch part of that discovery
+ *                         (Machine.swift:48-56 measures, never assumes)
  *   h3c_init/h3c_destroy  the backend instance AttentionRegistry.resolve
  *                         creates once per render (AttentionBackend.swift:255-259)
  */
@@ -50,7 +52,7 @@
 extern "C" {
 #endif
 
-#define H3C_ABI_VERSION 1
+#define H3C_ABI_VERSION 2
 
 typedef enum h3c_status {
   H3C_OK = 0,
@@ -74,10 +76,26 @@ typedef struct h3c_devinfo {
   int64_t hbm_free_bytes;
   int32_t max_smem_per_block_optin;
   int32_t l2_bytes;
-  int32_t peer_count;         /* devices this one can access peer-to-peer */
-  int32_t nvlink_peer_mask;   /* bit d set: device d is a P2P peer */
+  int32_t peer_count;         /* devices this one can access peer-to-peer (NVLink or PCIe) */
+  int32_t nvlink_peer_mask;   /* bit d set: device d is a P2P peer (cudaDeviceCanAccessPeer) */
   char name[96];
+  /* from NVML (read-only queries); -1 where NVML is not available */
+  int32_t nvlink_links;       /* active NVLink links of this device */
+  int32_t nvlink_version;     /* NVLink version NVML reports for the first active link */
+  int32_t nvswitch_links;     /* active links whose remote end is an NVSwitch */
+  int32_t native_atomic_peer_mask; /* bit d: P2P native atomics with device d (NVLink, not PCIe) */
+  char pci_bus_id[16];        /* "0000:1B:00.0" */
 } h3c_devinfo;
+
+/* NVLink state of one device, by PCI bus id (NVML through dlopen; nothing is
+ * changed).  available = 0 when NVML cannot be loaded. */
+typedef struct h3c_nvlink {
+  int32_t available;
+  int32_t links_active;
+  int32_t links_to_switch;
+  int32_t links_to_gpu;
+  int32_t version;            /* -1: unknown */
+} h3c_nvlink;
 
 /* Block-mask specification (128x128 blocks in raster token order).
  * Tokens [0, prefix_len) are the conditioning prefix (e.g. audio); tokens
@@ -138,6 +156,18 @@ h3c_status h3c_destroy(h3c_ctx* ctx);
 const char* h3c_last_error(const h3c_ctx* ctx);   /* never NULL */
 h3c_status h3c_device_info(h3c_ctx* ctx, h3c_devinfo* info);
 h3c_status h3c_device_count(int* count);
+/* NVLink links of the device at pci_bus_id: H3C_OK, H3C_ERR_NO_DEVICE (NVML
+ * does not know the bus id) or H3C_ERR_UNSUPPORTED (no NVML).  Needs no
+ * context and no CUDA call. */
+h3c_status h3c_nvlink_query(const char* pci_bus_id, h3c_nvlink* out);
+
+/* Device memory on the context's device, for hosts that bind no CUDA runtime
+ * of their own (a Swift host keeps its block list and RoPE table here).
+ * h3c_device_free(ctx, NULL) is a no-op.  The reference has no counterpart:
+ * MLX owns its buffers (Sources/H3Attention/AttentionBackend.swift:126-127
+ * takes MLXArrays). */
+h3c_status h3c_device_alloc(h3c_ctx* ctx, size_t bytes, void** out);
+h3c_status h3c_device_free(h3c_ctx* ctx, void* ptr);
 
 /* --- block mask ---------------------------------------------------------- */
 /* Host builder.  row_ptr: [n_blocks+1] or NULL; col_idx: capacity entries or

@@ -188,6 +188,28 @@ h3c_status h3c_destroy(h3c_ctx* ctx) {
   return H3C_OK;
 }
 
+h3c_status h3c_device_alloc(h3c_ctx* ctx, size_t bytes, void** out) {
+  if (!ctx || !out) return H3C_ERR_INVALID_ARGUMENT;
+  *out = nullptr;
+  H3_CUDA_TRY(ctx, cudaSetDevice(ctx->device));
+  if (bytes == 0) return H3C_OK;
+  cudaError_t e = cudaMalloc(out, bytes);
+  if (e == cudaErrorMemoryAllocation) {
+    cudaGetLastError();
+    return fail(ctx, H3C_ERR_CAPACITY, "h3c_device_alloc: out of device memory");
+  }
+  H3_CUDA_TRY(ctx, e);
+  return H3C_OK;
+}
+
+h3c_status h3c_device_free(h3c_ctx* ctx, void* ptr) {
+  if (!ctx) return H3C_ERR_INVALID_ARGUMENT;
+  if (!ptr) return H3C_OK;
+  H3_CUDA_TRY(ctx, cudaSetDevice(ctx->device));
+  H3_CUDA_TRY(ctx, cudaFree(ptr));
+  return H3C_OK;
+}
+
 const char* h3c_last_error(const h3c_ctx* ctx) { return ctx ? ctx->err.c_str() : kNullCtxError; }
 
 h3c_status h3c_device_info(h3c_ctx* ctx, h3c_devinfo* info) {
@@ -215,6 +237,21 @@ h3c_status h3c_device_info(h3c_ctx* ctx, h3c_devinfo* info) {
     }
   }
   std::memcpy(info->name, ctx->prop.name, sizeof(info->name) - 1);
+  for (int d = 0; d < n && d < 31; ++d) {
+    int atomics = 0;
+    if (d != ctx->device &&
+        cudaDeviceGetP2PAttribute(&atomics, cudaDevP2PAttrNativeAtomicSupported, ctx->device, d) == cudaSuccess &&
+        atomics)
+      info->native_atomic_peer_mask |= (1 << d);
+  }
+  H3_CUDA_TRY(ctx, cudaDeviceGetPCIBusId(info->pci_bus_id, (int)sizeof(info->pci_bus_id), ctx->device));
+  h3c_nvlink nv;
+  info->nvlink_links = info->nvlink_version = info->nvswitch_links = -1;
+  if (h3c_nvlink_query(info->pci_bus_id, &nv) == H3C_OK) {
+    info->nvlink_links = nv.links_active;
+    info->nvlink_version = nv.version;
+    info->nvswitch_links = nv.links_to_switch;
+  }
   return H3C_OK;
 }
 

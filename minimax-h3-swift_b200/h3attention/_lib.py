@@ -39,7 +39,8 @@ EXPORTS = (
     "h3c_prologue", "h3c_attn_fwd", "h3c_attn_workspace_size", "h3c_attn_fwd_sync",
     "h3c_fill_normal_bf16", "h3c_attn_fwd_noalloc", "h3c_device_status",
     "h3c_comm_unique_id", "h3c_comm_init", "h3c_comm_destroy", "h3c_attn_fwd_seqshard",
-    "h3c_blockmask_validate", "h3c_attn_fwd_noalloc_status",
+    "h3c_blockmask_validate", "h3c_attn_fwd_noalloc_status", "h3c_nvlink_query",
+    "h3c_device_alloc", "h3c_device_free",
 )
 
 
@@ -57,7 +58,14 @@ class DevInfo(C.Structure):
         ("sm_count", C.c_int32), ("hbm_bytes", C.c_int64), ("hbm_free_bytes", C.c_int64),
         ("max_smem_per_block_optin", C.c_int32), ("l2_bytes", C.c_int32),
         ("peer_count", C.c_int32), ("nvlink_peer_mask", C.c_int32), ("name", C.c_char * 96),
+        ("nvlink_links", C.c_int32), ("nvlink_version", C.c_int32), ("nvswitch_links", C.c_int32),
+        ("native_atomic_peer_mask", C.c_int32), ("pci_bus_id", C.c_char * 16),
     ]
+
+
+class NvLink(C.Structure):
+    _fields_ = [("available", C.c_int32), ("links_active", C.c_int32), ("links_to_switch", C.c_int32),
+                ("links_to_gpu", C.c_int32), ("version", C.c_int32)]
 
 
 class MaskSpec(C.Structure):
@@ -149,6 +157,9 @@ def load() -> C.CDLL:
             "h3c_attn_fwd_seqshard": ([vp, C.POINTER(AttnArgs), vp], st),
             "h3c_attn_fwd_noalloc": ([C.POINTER(AttnArgs), vp, C.c_char_p, C.c_size_t], st),
             "h3c_attn_fwd_noalloc_status": ([], st),
+            "h3c_nvlink_query": ([C.c_char_p, C.POINTER(NvLink)], st),
+            "h3c_device_alloc": ([vp, C.c_size_t, C.POINTER(vp)], st),
+            "h3c_device_free": ([vp, vp], st),
             "h3c_blockmask_validate": ([vp, vp, vp, i32, i64, vp], st),
         }
         for name, (args, res) in sig.items():

@@ -69,6 +69,7 @@ class Runtime:
         self._check(self.L.h3c_device_info(self.ctx, C.byref(info)))
         d = {f: getattr(info, f) for f, _ in _lib.DevInfo._fields_}
         d["name"] = info.name.decode()
+        d["pci_bus_id"] = info.pci_bus_id.decode()
         return d
 
     # ------------------------------------------------------------ attention

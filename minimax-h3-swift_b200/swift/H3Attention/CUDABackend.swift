@@ -9,6 +9,18 @@ import H3Foundation
 import H3Hardware
 import CH3Cuda
 
+/// What the host's CUDA build of MLX provides to this backend: the device
+/// address of an array's buffer and the stream MLX enqueues on.  MLX's Swift
+/// API exposes neither, so the host sets `CUDABackend.bridge` once at
+/// start-up; without a bridge the backend reports itself unavailable and the
+/// registry refuses it (never a silent downgrade).
+package protocol H3CUDADeviceBridge: Sendable {
+    /// Device pointer of a contiguous, evaluated array (row-major).
+    func devicePointer(_ array: MLXArray) -> UnsafeMutableRawPointer?
+    /// The cudaStream_t MLX is using on this thread (nil: the default stream).
+    func currentStream() -> UnsafeMutableRawPointer?
+}
+
 /// Block-sparse attention over a per-render compacted 128x128 block list.
 ///
 /// Declines (returns nil, so the caller runs dense) when no render layout
@@ -21,9 +33,12 @@ package final class CUDABackend: H3AttentionBackend, @unchecked Sendable {
     package static let materialisesScores = false
     package static let prefersMortonOrder = false
 
+    /// Set by the host before the registry resolves a backend.
+    nonisolated(unsafe) package static var bridge: H3CUDADeviceBridge?
+
     package static func isAvailable(on machine: Machine) -> Bool {
         var n: Int32 = 0
-        return h3c_device_count(&n) == H3C_OK && n > 0
+        return bridge != nil && h3c_device_count(&n) == H3C_OK && n > 0
     }
 
     private var ctx: OpaquePointer?
@@ -39,27 +54,38 @@ package final class CUDABackend: H3AttentionBackend, @unchecked Sendable {
     }
 
     deinit {
-        if let rowPtr { cudaFreeBridge(rowPtr) }
-        if let colIdx { cudaFreeBridge(colIdx) }
-        if let ropeTable { cudaFreeBridge(ropeTable) }
-        if let ctx { h3c_destroy(ctx) }
+        if let ctx {
+            h3c_device_free(ctx, rowPtr)
+            h3c_device_free(ctx, colIdx)
+            h3c_device_free(ctx, ropeTable)
+            h3c_destroy(ctx)
+        }
     }
 
-    /// Builds the render's block list once (AttentionContext has no geometry).
+    private func fail(_ feature: String) -> H3Error {
+        H3Error.unavailableFeature(feature: feature, detail: ctx.map { String(cString: h3c_last_error($0)) } ?? "no device")
+    }
+
+    /// Builds the render's block list once (AttentionContext has no geometry)
+    /// into library-owned device memory, and validates it.
     package func prepareRender(spec: h3c_mask_spec) throws {
+        guard let ctx else { throw fail("b200 block list") }
         var s = spec
         var nnz: Int64 = 0
         guard h3c_blockmask_build(&s, nil, nil, 0, &nnz) == H3C_OK else {
             throw H3Error.unavailableFeature(feature: "b200 block list", detail: "invalid mask spec")
         }
         let nb = Int((spec.seq_len + spec.block - 1) / spec.block)
-        rowPtr = cudaMallocBridge((nb + 1) * 4)
-        colIdx = cudaMallocBridge(Int(nnz) * 4)
-        guard let ctx, h3c_blockmask_build_device(ctx, &s, rowPtr?.assumingMemoryBound(to: Int32.self),
-                                                  colIdx?.assumingMemoryBound(to: Int32.self),
-                                                  nnz, &nnz, nil) == H3C_OK else {
-            throw H3Error.unavailableFeature(feature: "b200 block list", detail: "device build failed")
-        }
+        h3c_device_free(ctx, rowPtr); rowPtr = nil
+        h3c_device_free(ctx, colIdx); colIdx = nil
+        guard h3c_device_alloc(ctx, (nb + 1) * 4, &rowPtr) == H3C_OK,
+              h3c_device_alloc(ctx, max(Int(nnz), 1) * 4, &colIdx) == H3C_OK,
+              h3c_blockmask_build_device(ctx, &s, rowPtr?.assumingMemoryBound(to: Int32.self),
+                                         colIdx?.assumingMemoryBound(to: Int32.self), max(nnz, 1), &nnz,
+                                         nil) == H3C_OK,
+              h3c_blockmask_validate(ctx, rowPtr?.assumingMemoryBound(to: Int32.self),
+                                     colIdx?.assumingMemoryBound(to: Int32.self), Int32(nb), nnz, nil) == H3C_OK
+        else { throw fail("b200 block list") }
         seqLen = Int(spec.seq_len)
     }
 
@@ -68,6 +94,7 @@ package final class CUDABackend: H3AttentionBackend, @unchecked Sendable {
     /// `prepareRender` builds in H3Transformer.swift:263-276, for the fused
     /// prologue (H3C_FUSE_PROLOGUE with `a.rope_table` / `a.rope_half`).
     package func prepareRope(layout: h3c_layout_spec, invFreq: UnsafePointer<Float>, n: Int32) throws {
+        guard let ctx else { throw fail("b200 rope table") }
         var spec = layout
         var nseg: Int32 = 0
         var total: Int64 = 0
@@ -75,31 +102,74 @@ package final class CUDABackend: H3AttentionBackend, @unchecked Sendable {
         guard h3c_packed_layout(&spec, nil, 0, &nseg, &total, &err, err.count) == H3C_OK else {
             throw H3Error.unavailableFeature(feature: "b200 rope table", detail: String(cString: err))
         }
-        ropeTable = cudaMallocBridge(Int(total) * Int(3 * n) * 8)
-        guard let ctx, h3c_rope_table_layout(ctx, &spec, invFreq, n, ropeTable, total, nil) == H3C_OK else {
-            throw H3Error.unavailableFeature(feature: "b200 rope table", detail: "device build failed")
-        }
+        h3c_device_free(ctx, ropeTable); ropeTable = nil
+        guard h3c_device_alloc(ctx, Int(total) * Int(3 * n) * 8, &ropeTable) == H3C_OK,
+              h3c_rope_table_layout(ctx, &spec, invFreq, n, ropeTable, total, nil) == H3C_OK
+        else { throw fail("b200 rope table") }
         ropeHalf = 3 * n
+    }
+
+    /// Shared by `attend` and `attendFused`: the call's operands as `[H, S, D]`
+    /// views, or nil when this call is declined.
+    private func args(_ queries: MLXArray, _ keys: MLXArray, _ values: MLXArray, _ out: MLXArray,
+                      scale: Float, context: AttentionContext) -> h3c_attn_args? {
+        guard let bridge = Self.bridge, rowPtr != nil, colIdx != nil,
+              queries.ndim == 3, queries.dim(-1) == 128, queries.dim(1) == seqLen,
+              context.sequenceLength == seqLen,
+              let qp = bridge.devicePointer(queries), let kp = bridge.devicePointer(keys),
+              let vp = bridge.devicePointer(values), let op = bridge.devicePointer(out) else { return nil }
+        func view(_ p: UnsafeMutableRawPointer) -> h3c_view {   // [H, S, D]
+            h3c_view(ptr: p, token_stride: 128, head_stride: Int64(seqLen * 128))
+        }
+        var a = h3c_attn_args()
+        a.q = view(qp); a.k = view(kp); a.v = view(vp); a.out = view(op)
+        a.seq_len = Int32(seqLen); a.heads = Int32(queries.dim(0)); a.head_dim = 128
+        a.head_offset = 0; a.head_count = a.heads
+        a.scale = scale; a.block = 128; a.flags = 0
+        a.row_ptr = UnsafePointer(rowPtr!.assumingMemoryBound(to: Int32.self))
+        a.col_idx = UnsafePointer(colIdx!.assumingMemoryBound(to: Int32.self))
+        return a
     }
 
     package func attend(queries: MLXArray, keys: MLXArray, values: MLXArray,
                         scale: Float, mask: MLXArray?, context: AttentionContext) -> MLXArray? {
-        guard mask == nil, let ctx, let rowPtr, let colIdx,
-              queries.ndim == 3, queries.dim(-1) == 128, queries.dim(1) == seqLen,
-              context.sequenceLength == seqLen else { return nil }
-        let heads = queries.dim(0)
+        guard mask == nil, let ctx else { return nil }
         let out = MLXArray.zeros(queries.shape, dtype: queries.dtype)
-        func view(_ a: MLXArray) -> h3c_view {   // [H, S, D]
-            h3c_view(ptr: devicePointer(a), token_stride: 128, head_stride: Int64(seqLen * 128))
+        eval(queries, keys, values, out)
+        guard var a = args(queries, keys, values, out, scale: scale, context: context),
+              h3c_attn_fwd(ctx, &a, Self.bridge?.currentStream()) == H3C_OK else { return nil }
+        return out
+    }
+
+    /// The fused entry (next to `attend`, as `AttentionLayer.callAsFunction`
+    /// would call it, Sources/H3Modules/DiTBlock.swift:346-352): `queries` and
+    /// `keys` are the PRE-norm per-head projections; the per-head RMSNorm
+    /// (`qNorm`/`kNorm` weights, `eps`, Modulation.swift:116-120) and the
+    /// render's split-half RoPE (from `prepareRope`; RMSNorm only when none
+    /// was prepared) run inside the call.  Same decline rules as `attend`.
+    package func attendFused(queries: MLXArray, keys: MLXArray, values: MLXArray, scale: Float,
+                             qNormWeight: MLXArray, kNormWeight: MLXArray, eps: Float,
+                             context: AttentionContext) -> MLXArray? {
+        guard let ctx, let bridge = Self.bridge, qNormWeight.dim(-1) == 128, kNormWeight.dim(-1) == 128 else {
+            return nil
         }
-        var a = h3c_attn_args()
-        a.q = view(queries); a.k = view(keys); a.v = view(values); a.out = view(out)
-        a.seq_len = Int32(seqLen); a.heads = Int32(heads); a.head_dim = 128
-        a.head_offset = 0; a.head_count = Int32(heads)
-        a.scale = scale; a.block = 128; a.flags = 0
-        a.row_ptr = UnsafePointer(rowPtr.assumingMemoryBound(to: Int32.self))
-        a.col_idx = UnsafePointer(colIdx.assumingMemoryBound(to: Int32.self))
-        guard h3c_attn_fwd(ctx, &a, currentStream()) == H3C_OK else { return nil }
+        let out = MLXArray.zeros(queries.shape, dtype: queries.dtype)
+        eval(queries, keys, values, out, qNormWeight, kNormWeight)
+        guard var a = args(queries, keys, values, out, scale: scale, context: context),
+              let wq = bridge.devicePointer(qNormWeight), let wk = bridge.devicePointer(kNormWeight) else {
+            return nil
+        }
+        a.flags = Int32(H3C_FUSE_PROLOGUE.rawValue)
+        a.q_norm_weight = UnsafeRawPointer(wq)
+        a.k_norm_weight = UnsafeRawPointer(wk)
+        a.eps = eps
+        if let ropeTable {
+            a.rope_table = UnsafeRawPointer(ropeTable)
+            a.rope_half = ropeHalf
+        } else {
+            a.flags |= Int32(H3C_NO_ROPE.rawValue)
+        }
+        guard h3c_attn_fwd(ctx, &a, bridge.currentStream()) == H3C_OK else { return nil }
         return out
     }
 }

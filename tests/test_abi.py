@@ -27,14 +27,15 @@ def test_header_and_exports(lib):
     assert declared == set(lib.EXPORTS)
     for name in declared:
         assert hasattr(L, name), name
-    assert L.h3c_abi_version() == 1
+    assert L.h3c_abi_version() == 2
 
 
 def test_struct_layout_matches_header(lib):
     # sizes computed by the C compiler for the same declarations
     assert C.sizeof(lib.MaskSpec) == 13 * 4 + 4 + 8
     assert C.sizeof(lib.View) == 24
-    assert C.sizeof(lib.DevInfo) == 4 * 4 + 16 + 4 * 4 + 96
+    assert C.sizeof(lib.DevInfo) == 4 * 4 + 16 + 4 * 4 + 96 + 4 * 4 + 16
+    assert C.sizeof(lib.NvLink) == 5 * 4
     assert C.sizeof(lib.RefBlock) == 20 and C.sizeof(lib.Segment) == 12
     assert C.sizeof(lib.LayoutSpec) == 8 * 4 + 8 + 8 + 8
 
@@ -109,3 +110,27 @@ def test_density_targets():
     assert 0.20 < d1 < 0.30
     assert 0.08 < d2 < 0.13
     assert BlockList.build(CONFIGS["config4"].mask_spec()).density == 1.0
+
+
+def test_nvlink_discovery_against_a_stand_in_nvml(lib, tmp_path):
+    """h3c_nvlink_query parses NVML's answers (read-only queries) into link,
+    NVSwitch and version counts; checked with a stand-in NVML built from
+    tests/c/fake_nvml.c, since this machine has no GPU."""
+    import subprocess
+
+    so = tmp_path / "libfake_nvml.so"
+    subprocess.run(["gcc", "-shared", "-fPIC", "-O1", "-o", str(so), os.path.join(ROOT, "tests", "c", "fake_nvml.c")],
+                   check=True)
+    os.environ["H3C_NVML_LIB"] = str(so)
+    try:
+        L = lib.load()
+        nv = lib.NvLink()
+        assert L.h3c_nvlink_query(b"0000:1B:00.0", C.byref(nv)) == lib.H3C_OK
+        assert (nv.available, nv.links_active, nv.links_to_switch, nv.links_to_gpu, nv.version) == (1, 18, 17, 1, 5)
+        assert L.h3c_nvlink_query(b"0000:99:00.0", C.byref(nv)) == lib.H3C_ERR_NO_DEVICE
+        os.environ["H3C_NVML_LIB"] = str(tmp_path / "missing.so")
+        assert L.h3c_nvlink_query(b"0000:1B:00.0", C.byref(nv)) == lib.H3C_ERR_UNSUPPORTED
+        assert nv.available == 0
+        assert L.h3c_nvlink_query(None, C.byref(nv)) == lib.H3C_ERR_INVALID_ARGUMENT
+    finally:
+        del os.environ["H3C_NVML_LIB"]

@@ -55,7 +55,7 @@ def test_host_half_matches_python(exe):
     want = 0
     for c in bl.col_idx.tolist():
         want = (want * 1000003 + c) % (1 << 64)
-    assert (abi, total, prefix, nb, nnz, check) == (1, lay.total_tokens, spec.prefix_len, bl.n_blocks, bl.nnz, want)
+    assert (abi, total, prefix, nb, nnz, check) == (2, lay.total_tokens, spec.prefix_len, bl.n_blocks, bl.nnz, want)
     segs = re.search(r"segments (\d+):(.*)", r.stdout)
     got = [tuple(int(x) for x in t) for t in re.findall(r"\((\d+),(\d+),(\d+)\)", segs.group(2))]
     kinds = ("text", "cond", "ref_img", "ref_audio", "audio", "video")

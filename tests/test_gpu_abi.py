@@ -68,3 +68,43 @@ def test_workspace_grows_under_a_call_on_another_stream(gpu):
                     k_norm=w, eps=1e-6)
         torch.cuda.synchronize()
         assert torch.equal(o, want)
+
+
+def test_device_info_reports_nvlink(gpu):
+    """h3c_device_info on a B200: SM count and HBM from CUDA, NVLink links,
+    version and NVSwitch links from NVML (read-only), P2P peers with native
+    atomics (NVLink, not PCIe) from CUDA.  Printed for the record."""
+    import torch
+
+    from h3attention import Runtime
+
+    info = Runtime.get(0).device_info()
+    print({k: info[k] for k in ("name", "pci_bus_id", "sm_count", "hbm_bytes", "peer_count", "nvlink_links",
+                                "nvlink_version", "nvswitch_links", "nvlink_peer_mask", "native_atomic_peer_mask")})
+    assert info["cc_major"] == 10 and info["sm_count"] >= 100
+    assert info["pci_bus_id"].count(":") == 2
+    assert -1 <= info["nvlink_links"] <= 18
+    if info["nvlink_links"] > 0:
+        assert info["nvlink_version"] >= 1
+        assert 0 <= info["nvswitch_links"] <= info["nvlink_links"]
+    n = torch.cuda.device_count()
+    assert info["peer_count"] <= n - 1
+    # native atomics between peers only over NVLink: a subset of the P2P peers
+    assert info["native_atomic_peer_mask"] & ~info["nvlink_peer_mask"] == 0
+
+
+def test_device_alloc_and_free(gpu):
+    """h3c_device_alloc / h3c_device_free (device memory for hosts without a
+    CUDA runtime binding): a buffer the kernels can use, freed again."""
+    import ctypes as C
+
+    from h3attention import Runtime, _lib
+
+    rt = Runtime.get(0)
+    L = _lib.load()
+    p = C.c_void_p()
+    assert L.h3c_device_alloc(rt.ctx, 1 << 20, C.byref(p)) == _lib.H3C_OK and p.value
+    assert L.h3c_device_free(rt.ctx, p) == _lib.H3C_OK
+    assert L.h3c_device_free(rt.ctx, None) == _lib.H3C_OK
+    q = C.c_void_p(1)
+    assert L.h3c_device_alloc(rt.ctx, 0, C.byref(q)) == _lib.H3C_OK and not q.value
