@@ -314,6 +314,17 @@ h3c_status h3c_comm_destroy(h3c_ctx* ctx);   /* also done by h3c_destroy */
  * nothing in the reference (AttentionLayer.sdpa is single-device,
  * Sources/H3Modules/DiTBlock.swift:293-328). */
 h3c_status h3c_attn_fwd_seqshard(h3c_ctx* ctx, const h3c_attn_args* args, void* stream);
+/* Bounded wait for the work enqueued on `stream` (an h3c_attn_fwd_seqshard
+ * call): H3C_OK once it is done; H3C_ERR_NCCL when NCCL reports an error;
+ * H3C_ERR_TIMEOUT when it is not done after timeout_ms (a rank that never
+ * took part): the communicator is then aborted (its kernels stop), the
+ * call's output is invalid and the context's other calls stay usable;
+ * h3c_comm_destroy + h3c_comm_init make a new communicator.  The
+ * communicator is non-blocking when the process's NCCL supports it (2.14+);
+ * with an older NCCL a timeout is reported but cannot be aborted.
+ * Replaces the reference's render-level cancellation
+ * (Sources/MiniMaxH3/RenderEngine.swift:574-590) for the exchange. */
+h3c_status h3c_comm_wait(h3c_ctx* ctx, void* stream, int64_t timeout_ms);
 
 /* --- synthetic inputs ------------------------------------------------------ */
 /* Counter-based N(mean, std) bf16 generator; element i is a function of

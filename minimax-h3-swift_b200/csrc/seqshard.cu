@@ -12,12 +12,22 @@
 // NCCL is opened with dlopen when a communicator is first created, reusing a
 // libnccl.so.2 that the process has already loaded (for example PyTorch's),
 // so the library has no link-time NCCL dependency.
+//
+// Failure detection: the communicator is created non-blocking when the NCCL
+// in the process supports it (ncclCommInitRankConfig, 2.14+), and
+// h3c_comm_wait bounds every wait on the exchange: it polls the stream and
+// ncclCommGetAsyncError against a deadline and, when a peer never arrives,
+// aborts the communicator (ncclCommAbort stops its kernels) and returns
+// H3C_ERR_TIMEOUT instead of hanging -- the kernel-level counterpart of the
+// reference's render cancellation (Sources/MiniMaxH3/RenderEngine.swift:
+// 574-590).
 #include <dlfcn.h>
+#include <time.h>
 
+#include <climits>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
-
-#include <cstdlib>
 
 #include "common.cuh"
 
@@ -30,6 +40,35 @@ typedef struct {
   char internal[128];
 } ncclUniqueId_;
 enum { kNcclBfloat16 = 9 };  // ncclBfloat16
+constexpr int kNcclSuccess = 0, kNcclInProgress = 7;
+
+// ncclConfig_t as nccl.h 2.28 lays it out (fields are only ever appended;
+// `size` and `version` tell the library how many of them it was given).
+struct NcclConfig {
+  size_t size;
+  unsigned int magic;
+  unsigned int version;
+  int blocking, cgaClusterSize, minCTAs, maxCTAs;
+  const char* netName;
+  int splitShare, trafficClass;
+  const char* commName;
+  int collnetEnable, CTAPolicy, shrinkShare, nvlsCTAs, nChannelsPerNetPeer, nvlinkCentricSched;
+};
+
+NcclConfig nonblocking_config(int runtime_version) {
+  NcclConfig c;
+  c.size = sizeof(NcclConfig);
+  c.magic = 0xcafebeef;
+  // the struct above is 2.28's; an older library reads the prefix it knows
+  c.version = (unsigned)(runtime_version < 22809 ? runtime_version : 22809);
+  c.blocking = 0;
+  c.cgaClusterSize = c.minCTAs = c.maxCTAs = INT_MIN;  // NCCL_CONFIG_UNDEF_INT
+  c.netName = nullptr;
+  c.splitShare = c.trafficClass = INT_MIN;
+  c.commName = nullptr;
+  c.collnetEnable = c.CTAPolicy = c.shrinkShare = c.nvlsCTAs = c.nChannelsPerNetPeer = c.nvlinkCentricSched = INT_MIN;
+  return c;
+}
 
 struct Nccl {
   ncclResult_t_ (*GetUniqueId)(ncclUniqueId_*);
@@ -40,6 +79,12 @@ struct Nccl {
   ncclResult_t_ (*Send)(const void*, size_t, int, int, ncclComm_t_, cudaStream_t);
   ncclResult_t_ (*Recv)(void*, size_t, int, int, ncclComm_t_, cudaStream_t);
   const char* (*GetErrorString)(ncclResult_t_);
+  // optional (non-blocking communicators, bounded waits)
+  ncclResult_t_ (*CommInitRankConfig)(ncclComm_t_*, int, ncclUniqueId_, int, NcclConfig*) = nullptr;
+  ncclResult_t_ (*CommGetAsyncError)(ncclComm_t_, ncclResult_t_*) = nullptr;
+  ncclResult_t_ (*CommAbort)(ncclComm_t_) = nullptr;
+  ncclResult_t_ (*CommFinalize)(ncclComm_t_) = nullptr;
+  ncclResult_t_ (*GetVersion)(int*) = nullptr;
   bool ok = false;
 };
 
@@ -58,6 +103,11 @@ Nccl* nccl() {
     n.Send = (decltype(n.Send))dlsym(h, "ncclSend");
     n.Recv = (decltype(n.Recv))dlsym(h, "ncclRecv");
     n.GetErrorString = (decltype(n.GetErrorString))dlsym(h, "ncclGetErrorString");
+    n.CommInitRankConfig = (decltype(n.CommInitRankConfig))dlsym(h, "ncclCommInitRankConfig");
+    n.CommGetAsyncError = (decltype(n.CommGetAsyncError))dlsym(h, "ncclCommGetAsyncError");
+    n.CommAbort = (decltype(n.CommAbort))dlsym(h, "ncclCommAbort");
+    n.CommFinalize = (decltype(n.CommFinalize))dlsym(h, "ncclCommFinalize");
+    n.GetVersion = (decltype(n.GetVersion))dlsym(h, "ncclGetVersion");
     n.ok = n.GetUniqueId && n.CommInitRank && n.CommDestroy && n.GroupStart && n.GroupEnd && n.Send && n.Recv &&
            n.GetErrorString;
   });
@@ -67,6 +117,21 @@ Nccl* nccl() {
 h3c_status fail(h3c_ctx* ctx, h3c_status st, const std::string& msg) {
   if (ctx) ctx->err = msg;
   return st;
+}
+
+// A call on a non-blocking communicator may return ncclInProgress: the
+// operation is being set up in the background and counts as issued.
+bool issued(ncclResult_t_ r) { return r == kNcclSuccess || r == kNcclInProgress; }
+
+double now_ms() {
+  timespec t;
+  clock_gettime(CLOCK_MONOTONIC, &t);
+  return t.tv_sec * 1e3 + t.tv_nsec * 1e-6;
+}
+
+void nap() {
+  timespec t{0, 100000};  // 100 us between polls
+  nanosleep(&t, nullptr);
 }
 
 // One head chunk of the exchange: heads [h0, h0 + hc) of every rank's group
@@ -98,6 +163,8 @@ constexpr int kDefaultChunks = 1;
 
 struct h3c_comm_state {
   ncclComm_t_ comm = nullptr;
+  bool nonblocking = false;
+  bool aborted = false;  // after a timeout: the communicator is gone, init again
   int nranks = 0, rank = 0;
   void* buf = nullptr;
   size_t buf_bytes = 0;
@@ -135,8 +202,34 @@ h3c_status h3c_comm_init(h3c_ctx* ctx, const h3c_comm_id* id, int nranks, int ra
   ncclUniqueId_ uid;
   std::memcpy(uid.internal, id->internal, sizeof(uid.internal));
   auto* st = new h3c_comm_state();
-  ncclResult_t_ r = n->CommInitRank(&st->comm, nranks, uid, rank);
+  ncclResult_t_ r;
+  int ver = 0;
+  if (n->CommInitRankConfig && n->CommGetAsyncError && n->CommAbort && n->GetVersion && n->GetVersion(&ver) == 0 &&
+      ver >= 21400) {
+    NcclConfig cfg = nonblocking_config(ver);
+    r = n->CommInitRankConfig(&st->comm, nranks, uid, rank, &cfg);
+    st->nonblocking = true;
+    // a non-blocking init completes in the background: wait for it, bounded
+    const char* e = getenv("H3C_NCCL_INIT_TIMEOUT_MS");
+    const double limit = e ? atof(e) : 300000.0;
+    const double t0 = now_ms();
+    while (r == kNcclInProgress && st->comm) {
+      ncclResult_t_ a = kNcclInProgress;
+      n->CommGetAsyncError(st->comm, &a);
+      r = a;
+      if (r != kNcclInProgress) break;
+      if (now_ms() - t0 > limit) {
+        n->CommAbort(st->comm);
+        delete st;
+        return fail(ctx, H3C_ERR_TIMEOUT, "h3c_comm_init: the other ranks did not join in time (communicator aborted)");
+      }
+      nap();
+    }
+  } else {
+    r = n->CommInitRank(&st->comm, nranks, uid, rank);
+  }
   if (r != 0) {
+    if (st->comm && st->nonblocking) n->CommAbort(st->comm);
     delete st;
     return fail(ctx, H3C_ERR_NCCL, std::string("ncclCommInitRank: ") + n->GetErrorString(r));
   }
@@ -174,7 +267,22 @@ h3c_status h3c_comm_destroy(h3c_ctx* ctx) {
     if (st->attn_done[c]) cudaEventDestroy(st->attn_done[c]);
   }
   Nccl* n = nccl();
-  if (n && st->comm) n->CommDestroy(st->comm);
+  if (n && st->comm && !st->aborted) {
+    bool done = true;
+    if (st->nonblocking && n->CommFinalize) {
+      // a non-blocking communicator finalises in the background (bounded);
+      // one that does not finish is aborted instead of destroyed
+      ncclResult_t_ r = n->CommFinalize(st->comm);
+      const double t0 = now_ms();
+      while (r == kNcclInProgress && now_ms() - t0 < 30000.0) {
+        nap();
+        n->CommGetAsyncError(st->comm, &r);
+      }
+      done = r == kNcclSuccess;
+    }
+    if (done) n->CommDestroy(st->comm);
+    else n->CommAbort(st->comm);
+  }
   delete st;
   ctx->comm = nullptr;
   return H3C_OK;
@@ -199,6 +307,8 @@ h3c_status h3c_attn_fwd_seqshard(h3c_ctx* ctx, const h3c_attn_args* args, void* 
       return fail(ctx, H3C_ERR_INVALID_ARGUMENT, "h3c_attn_fwd_seqshard: q/k/v/out need 16-byte aligned rows");
   Nccl* n = nccl();
   if (!n) return fail(ctx, H3C_ERR_NCCL, "h3c_attn_fwd_seqshard: NCCL unavailable");
+  if (st->aborted)
+    return fail(ctx, H3C_ERR_NCCL, "h3c_attn_fwd_seqshard: the communicator was aborted; h3c_comm_destroy and init again");
   H3_CUDA_TRY(ctx, cudaSetDevice(ctx->device));
   cudaStream_t s = (cudaStream_t)stream;
 
@@ -245,15 +355,15 @@ h3c_status h3c_attn_fwd_seqshard(h3c_ctx* ctx, const h3c_attn_args* args, void* 
   cudaStream_t x = st->side;
 
   auto exchange = [&](uint16_t* src, uint16_t* dst, size_t per_peer) -> h3c_status {
-    if (n->GroupStart() != 0) return fail(ctx, H3C_ERR_NCCL, "ncclGroupStart");
+    if (!issued(n->GroupStart())) return fail(ctx, H3C_ERR_NCCL, "ncclGroupStart");
     for (int p = 0; p < P; ++p) {
-      if (n->Send(src + p * per_peer, per_peer, kNcclBfloat16, p, st->comm, x) != 0 ||
-          n->Recv(dst + p * per_peer, per_peer, kNcclBfloat16, p, st->comm, x) != 0) {
+      if (!issued(n->Send(src + p * per_peer, per_peer, kNcclBfloat16, p, st->comm, x)) ||
+          !issued(n->Recv(dst + p * per_peer, per_peer, kNcclBfloat16, p, st->comm, x))) {
         n->GroupEnd();
         return fail(ctx, H3C_ERR_NCCL, "ncclSend/ncclRecv");
       }
     }
-    if (n->GroupEnd() != 0) return fail(ctx, H3C_ERR_NCCL, "ncclGroupEnd");
+    if (!issued(n->GroupEnd())) return fail(ctx, H3C_ERR_NCCL, "ncclGroupEnd");
     return H3C_OK;
   };
   auto chunk_of = [&](int c, int* h0, int* hc) {
@@ -315,6 +425,43 @@ h3c_status h3c_attn_fwd_seqshard(h3c_ctx* ctx, const h3c_attn_args* args, void* 
   H3_CUDA_TRY(ctx, cudaEventRecord(st->out_done, x));
   H3_CUDA_TRY(ctx, cudaStreamWaitEvent(s, st->out_done, 0));
   return H3C_OK;
+}
+
+h3c_status h3c_comm_wait(h3c_ctx* ctx, void* stream, int64_t timeout_ms) {
+  if (!ctx || timeout_ms < 0) return H3C_ERR_INVALID_ARGUMENT;
+  h3c_comm_state* st = comm_of(ctx);
+  if (!st) return fail(ctx, H3C_ERR_INVALID_ARGUMENT, "h3c_comm_wait: no communicator");
+  if (st->aborted) return fail(ctx, H3C_ERR_NCCL, "h3c_comm_wait: the communicator was aborted");
+  Nccl* n = nccl();
+  H3_CUDA_TRY(ctx, cudaSetDevice(ctx->device));
+  cudaStream_t s = (cudaStream_t)stream;
+  const double t0 = now_ms();
+  auto abort_comm = [&]() {
+    if (n && n->CommAbort) n->CommAbort(st->comm);  // stops the communicator's kernels
+    st->aborted = true;
+  };
+  while (true) {
+    const cudaError_t q = cudaStreamQuery(s);
+    ncclResult_t_ a = kNcclSuccess;
+    if (st->nonblocking && n->CommGetAsyncError) n->CommGetAsyncError(st->comm, &a);
+    if (a != kNcclSuccess && a != kNcclInProgress) {
+      abort_comm();
+      return fail(ctx, H3C_ERR_NCCL, std::string("h3c_comm_wait: NCCL reported ") + n->GetErrorString(a));
+    }
+    if (q == cudaSuccess) return H3C_OK;
+    if (q != cudaErrorNotReady) H3_CUDA_TRY(ctx, q);
+    if (now_ms() - t0 > (double)timeout_ms) break;
+    nap();
+  }
+  if (!st->nonblocking || !n->CommAbort)
+    return fail(ctx, H3C_ERR_TIMEOUT, "h3c_comm_wait: timed out (blocking communicator: cannot abort)");
+  abort_comm();
+  // the aborted exchange kernels return; let the stream drain (bounded)
+  const double t1 = now_ms();
+  while (cudaStreamQuery(s) == cudaErrorNotReady && now_ms() - t1 < (double)timeout_ms + 10000.0) nap();
+  return fail(ctx, H3C_ERR_TIMEOUT,
+              "h3c_comm_wait: a peer did not take part in time; the communicator was aborted (output invalid; "
+              "h3c_comm_destroy and h3c_comm_init to continue)");
 }
 
 }  // extern "C"

@@ -40,7 +40,7 @@ EXPORTS = (
     "h3c_fill_normal_bf16", "h3c_attn_fwd_noalloc", "h3c_device_status",
     "h3c_comm_unique_id", "h3c_comm_init", "h3c_comm_destroy", "h3c_attn_fwd_seqshard",
     "h3c_blockmask_validate", "h3c_attn_fwd_noalloc_status", "h3c_nvlink_query",
-    "h3c_device_alloc", "h3c_device_free",
+    "h3c_device_alloc", "h3c_device_free", "h3c_comm_wait",
 )
 
 
@@ -159,6 +159,7 @@ def load() -> C.CDLL:
             "h3c_attn_fwd_noalloc_status": ([], st),
             "h3c_nvlink_query": ([C.c_char_p, C.POINTER(NvLink)], st),
             "h3c_device_alloc": ([vp, C.c_size_t, C.POINTER(vp)], st),
+            "h3c_comm_wait": ([vp, vp, i64], st),
             "h3c_device_free": ([vp, vp], st),
             "h3c_blockmask_validate": ([vp, vp, vp, i32, i64, vp], st),
         }

@@ -125,12 +125,23 @@ class Runtime:
         C.memmove(C.addressof(cid), unique_id, 128)
         self._check(self.L.h3c_comm_init(self.ctx, C.byref(cid), nranks, rank))
 
-    def attn_fwd_seqshard(self, *, stream=None, **kw):
-        """This rank's [S_r, H, D] shards in and out; ``seq_len`` is global."""
+    def attn_fwd_seqshard(self, *, stream=None, timeout_ms=None, **kw):
+        """This rank's [S_r, H, D] shards in and out; ``seq_len`` is global.
+        With ``timeout_ms`` the call also waits (bounded) for the exchange:
+        a rank that does not take part raises H3CError(H3C_ERR_TIMEOUT) after
+        the communicator is aborted, instead of hanging."""
         seq_len = kw.pop("seq_len")
         a = self.attn_args(**kw)
         a.seq_len = seq_len
         self._check(self.L.h3c_attn_fwd_seqshard(self.ctx, C.byref(a), _stream_ptr(stream)))
+        if timeout_ms is not None:
+            self.comm_wait(stream, timeout_ms)
+
+    def comm_wait(self, stream=None, timeout_ms: int = 60000):
+        self._check(self.L.h3c_comm_wait(self.ctx, _stream_ptr(stream), int(timeout_ms)))
+
+    def comm_destroy(self):
+        self._check(self.L.h3c_comm_destroy(self.ctx))
 
     def device_status(self):
         self._check(self.L.h3c_device_status(self.ctx))

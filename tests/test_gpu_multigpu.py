@@ -148,3 +148,99 @@ def test_c_abi_seqshard_two_gpus(gpu, chunks):
                 p.kill()
     for rank, err in res:
         assert err == 0.0, (rank, err)
+
+
+def _timeout_worker(rank, world, id_q, q_out, done_q):
+    try:
+        _timeout_body(rank, world, id_q, q_out, done_q)
+    except Exception as e:  # report instead of leaving the parent waiting
+        q_out.put((rank, repr(e)))
+
+
+def _timeout_body(rank, world, id_q, q_out, done_q):
+    import sys
+    import time
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    sys.path[:0] = [root, os.path.join(root, "minimax-h3-swift_b200")]
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    import torch
+
+    from h3attention import BlockList, H3CError, Runtime, _lib
+    from h3attention.configs import CONFIGS
+    from h3attention.sharding import seq_shard_len
+
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    wl = CONFIGS["config1"]
+    S, H = wl.seq_len, wl.heads
+    rt = Runtime.get(rank)
+    if rank == 0:  # rank 0 creates the NCCL id and hands it to rank 1
+        uid = Runtime.comm_unique_id()
+        id_q.put(uid)
+    else:
+        uid = id_q.get(timeout=60)
+    n = seq_shard_len(S, world)
+    mine = [rt.fill_normal(torch.empty((n, H, 128), dtype=torch.bfloat16, device=dev), 7 + rank, st)
+            for st in (1, 2, 3)]
+    bl = BlockList.build(wl.mask_spec())
+    rt.comm_init(uid, world, rank)
+    out = torch.empty_like(mine[0])
+    kw = dict(q=mine[0], k=mine[1], v=mine[2], out=out, layout="SHD", scale=128 ** -0.5, blocks=bl.on(dev),
+              seq_len=S)
+    # step 1: both ranks take part; the bounded wait returns in time
+    rt.attn_fwd_seqshard(timeout_ms=60000, **kw)
+    if rank == 1:
+        # this rank leaves between steps: it never joins step 2 and waits
+        # (alive, its memory intact) until rank 0 has reported
+        q_out.put((1, "left after step 1"))
+        done_q.get(timeout=120)
+        os._exit(0)
+    # step 2 on rank 0 alone: the exchange cannot complete; the wait must
+    # give up after 2 s with H3C_ERR_TIMEOUT (communicator aborted)
+    t0 = time.time()
+    status = None
+    try:
+        rt.attn_fwd_seqshard(timeout_ms=2000, **kw)
+    except H3CError as e:
+        status = e.status
+    waited = time.time() - t0
+    # the context stays usable for the single-GPU call
+    want = torch.empty_like(mine[0])
+    rt.attn_fwd(q=mine[0], k=mine[1], v=mine[2], out=want, layout="SHD", scale=128 ** -0.5, blocks=bl.on(dev))
+    torch.cuda.synchronize()
+    rt.device_status()
+    ok_after = bool(torch.isfinite(want.float()).all().item())
+    rt.comm_destroy()
+    q_out.put((0, (status, waited, ok_after, _lib.H3C_ERR_TIMEOUT)))
+
+
+def test_c_abi_seqshard_peer_that_never_joins_times_out(gpu):
+    """Failure detection of the NCCL exchange without a GPU fault: rank 1
+    takes part in one step and then never joins the next (it stays alive).
+    Rank 0's bounded wait (h3c_comm_wait) gives up after 2 s, aborts the
+    communicator and reports H3C_ERR_TIMEOUT; the context still runs the
+    single-GPU call.  NVLS off, plain NCCL send/recv."""
+    import torch
+    import torch.multiprocessing as mp
+
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    ctx = mp.get_context("spawn")
+    q, id_q, done_q = ctx.Queue(), ctx.Queue(), ctx.Queue()
+    procs = [ctx.Process(target=_timeout_worker, args=(r, 2, id_q, q, done_q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    try:
+        res = dict(q.get(timeout=180) for _ in range(2))
+    finally:
+        done_q.put("done")
+        for p in procs:
+            p.join(timeout=60)
+            if p.is_alive():
+                p.kill()
+    assert res[1] == "left after step 1", res
+    status, waited, ok_after, timeout_code = res[0]
+    assert status == timeout_code, res
+    assert 1.5 <= waited <= 30.0, waited
+    assert ok_after
