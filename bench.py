@@ -262,7 +262,7 @@ def run_reference(args):
 # dram__bytes_write.sum) from one ncu capture of the config-2 workload at 8
 # heads, scaled to 40 heads by the heads processed; None for workloads
 # without a capture.
-TRAFFIC_BYTES = {"config2": 5.92e9}
+TRAFFIC_BYTES = {"config2": 5.94e9}
 
 
 def _timed(fn, steps):
@@ -471,7 +471,12 @@ def run_ours(args):
     # End to end through the public host-buffer call (h3attention.host):
     # pinned host [H, S, D] q/k/v in, fused call, pinned host output back,
     # every step; uploads, compute and downloads of head chunks overlap.
-    if seqm:
+    if args.no_e2e:
+        hq = hout = q[:0]
+
+        def e2e_step():
+            pass
+    elif seqm:
         hq, hk, hv = (t.cpu().pin_memory() for t in (q, k, v))
         hout = torch.empty(out.shape, dtype=bf).pin_memory()
 
@@ -493,9 +498,12 @@ def run_ours(args):
         def e2e_step():
             ha(hq, hk, hv, hout, blocks, scale, q_norm=wq, k_norm=wk, eps=EPS, rope_table=tab)
 
-    e2e_step()
-    torch.cuda.synchronize()
-    e2e_ms = _timed(e2e_step, max(2, min(args.steps, 5)))
+    if args.no_e2e:  # sweeps only: the line then carries no e2e figure
+        e2e_ms = float("nan")
+    else:
+        e2e_step()
+        torch.cuda.synchronize()
+        e2e_ms = _timed(e2e_step, max(2, min(args.steps, 5)))
     if ws > 1:
         t = torch.tensor([e2e_ms, attn_ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -514,8 +522,9 @@ def run_ours(args):
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": scaling,
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1) bf16; shapes of the workload)",
             "config": _config(wl, bl, ws, mode),
-            "e2e": {"value": job_flops / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": e2e_ms,
-                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+            "e2e": None if args.no_e2e else {"value": job_flops / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
+                                             "ms_per_step": e2e_ms, "h2d_bytes_per_step": h2d,
+                                             "d2h_bytes_per_step": d2h},
             "roofline": {"bound": "tensor", "kernel": "attn_tc_kernel", "achieved": achieved,
                          "peak": peaks["bf16_tflops"], "unit": "TFLOP/s", "frac": achieved / peaks["bf16_tflops"],
                          "frac_sustained": achieved / peaks["bf16_tflops_sustained"], "peak_source": src,
@@ -548,6 +557,7 @@ def main():
     ap.add_argument("--cpu-budget", type=float, default=15.0, help="seconds of CPU baseline sampling")
     ap.add_argument("--ref-budget", type=float, default=120.0, help="total seconds for --impl reference")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer pass (density/mode sweeps only)")
     ap.add_argument("--chunk-heads", type=int, default=2, help="heads per pipeline stage of the e2e host call")
     ap.add_argument("--heads", type=int, default=None,
                     help="override the workload's head count (small profiling cases only)")

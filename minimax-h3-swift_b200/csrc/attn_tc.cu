@@ -17,7 +17,9 @@
 //   warp 1      MMA issuer (the whole warp, one lane elected per instruction):
 //               S = Q K^T (SS), O += P V (TS),
 //               in the order PV0 S0 PV1 S1 per entry so the two tiles'
-//               softmax phases alternate
+//               softmax phases alternate; each PV starts once the softmax
+//               has stored P for keys 0-95 (p_half) and waits for the last
+//               32 keys (p_full) only before its last two steps
 //   warp 2      TMEM allocator (512 columns)
 //   warps 4-7   softmax + epilogue of tile 0 (thread = query row = TMEM lane)
 //   warps 8-11  softmax + epilogue of tile 1
@@ -55,6 +57,7 @@ struct __align__(8) Barriers {
   uint64_t kv_empty[kStages];
   uint64_t s_full[2];
   uint64_t p_full[2];
+  uint64_t p_half[2];   // P of the first 96 keys written (split hand-off)
   uint64_t o_full[2];
   uint32_t tmem_base;
   int32_t abort;
@@ -309,6 +312,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(smem_u32(&bars->q_full[t]), 1);
       mbar_init(smem_u32(&bars->s_full[t]), 1);
       mbar_init(smem_u32(&bars->p_full[t]), 128);
+      mbar_init(smem_u32(&bars->p_half[t]), 128);
       mbar_init(smem_u32(&bars->o_full[t]), 1);
     }
     for (int s = 0; s < kStages; ++s) {
@@ -440,7 +444,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int nst = t == 0 ? ns0 : ns1;
           const int other = t == 0 ? pend1 : pend0;
           const int e = pend;
-          if (!iwait(smem_u32(&bars->p_full[t]), (uint32_t)((nst - 1) & 1)))
+          // split hand-off: the first six PV steps (keys 0-95) need only
+          // p_half; p_full is awaited before the last two
+          if (!iwait(smem_u32(&bars->p_half[t]), (uint32_t)((nst - 1) & 1)))
             return false;
           tc_fence_after();
           const int item = 2 * e + 1;
@@ -450,9 +456,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           // carry: shared addresses stay below 2^18)
           const uint64_t vdesc = smem_desc(smem_u32(sKV + (item % kStages) * kTileBytes), kHalfBytes, 1024);
 #pragma unroll
-          for (int kk = 0; kk < 8; ++kk)
+          for (int kk = 0; kk < 8; ++kk) {
+            if (kk == 6) {
+              if (!iwait(smem_u32(&bars->p_full[t]), (uint32_t)((nst - 1) & 1))) return false;
+              tc_fence_after();
+            }
             mma_ts_w(tmem + 256 * t + 128, tmem + 256 * t + kk * 8, vdesc + (uint64_t)((kk * 2048) >> 4),
                    kIdPV, (nst > 1 || kk > 0) ? 1u : 0u);
+          }
           pend = -1;
           if (other != e) tc_commit_w(smem_u32(&bars->kv_empty[item % kStages]));
           return true;
@@ -600,6 +611,11 @@ __global__ void __launch_bounds__(kThreads, 1)
               pk[e] = pack_bf16(p0v, p1v);
             }
             H3_TMEM_ST16(tS + 16 * c, pk);
+            if (c == 2) {  // keys 0-95 of P are in TMEM: the first six PV steps may start
+              tmem_wait_st();
+              tc_fence_before();
+              mbar_arrive(smem_u32(&bars->p_half[t]));
+            }
           }
           l += __uint_as_float((uint32_t)sum2) + __uint_as_float((uint32_t)(sum2 >> 32));
           tmem_wait_st();
