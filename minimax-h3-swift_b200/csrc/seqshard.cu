@@ -360,10 +360,27 @@ h3c_status h3c_attn_fwd_seqshard(h3c_ctx* ctx, const h3c_attn_args* args, void* 
       if (!issued(n->Send(src + p * per_peer, per_peer, kNcclBfloat16, p, st->comm, x)) ||
           !issued(n->Recv(dst + p * per_peer, per_peer, kNcclBfloat16, p, st->comm, x))) {
         n->GroupEnd();
-        return fail(ctx, H3C_ERR_NCCL, "ncclSend/ncclRecv");
+        ncclResult_t_ a = kNcclSuccess;
+        if (st->nonblocking) n->CommGetAsyncError(st->comm, &a);
+        return fail(ctx, H3C_ERR_NCCL, std::string("ncclSend/ncclRecv (communicator state: ") + n->GetErrorString(a) + ")");
       }
     }
-    if (!issued(n->GroupEnd())) return fail(ctx, H3C_ERR_NCCL, "ncclGroupEnd");
+    ncclResult_t_ r = n->GroupEnd();
+    if (!issued(r)) return fail(ctx, H3C_ERR_NCCL, std::string("ncclGroupEnd: ") + n->GetErrorString(r));
+    if (r == kNcclInProgress) {
+      // a non-blocking communicator launches the group in the background;
+      // it must settle before the next NCCL call on it (bounded)
+      const double t0 = now_ms();
+      while (r == kNcclInProgress) {
+        n->CommGetAsyncError(st->comm, &r);
+        if (r == kNcclInProgress && now_ms() - t0 > 60000.0) {
+          n->CommAbort(st->comm);
+          st->aborted = true;
+          return fail(ctx, H3C_ERR_TIMEOUT, "h3c_attn_fwd_seqshard: the exchange could not be launched (aborted)");
+        }
+      }
+      if (r != kNcclSuccess) return fail(ctx, H3C_ERR_NCCL, std::string("ncclGroupEnd: ") + n->GetErrorString(r));
+    }
     return H3C_OK;
   };
   auto chunk_of = [&](int c, int* h0, int* hc) {
