@@ -321,7 +321,11 @@ h3c_status h3c_attn_fwd_seqshard(h3c_ctx* ctx, const h3c_attn_args* args, void* 
  * call's output is invalid and the context's other calls stay usable;
  * h3c_comm_destroy + h3c_comm_init make a new communicator.  The
  * communicator is non-blocking when the process's NCCL supports it (2.14+);
- * with an older NCCL a timeout is reported but cannot be aborted.
+ * with an older NCCL, or with H3C_NCCL_BLOCKING=1 in the environment at
+ * h3c_comm_init, a timeout is reported but cannot be aborted.  The
+ * non-blocking communicator launches each exchange from NCCL's background
+ * thread: measured at 8 B200 on config 2, 18.5 ms per sequence-sharded call
+ * against 11.7 ms with a blocking one.
  * Replaces the reference's render-level cancellation
  * (Sources/MiniMaxH3/RenderEngine.swift:574-590) for the exchange. */
 h3c_status h3c_comm_wait(h3c_ctx* ctx, void* stream, int64_t timeout_ms);

@@ -204,8 +204,11 @@ h3c_status h3c_comm_init(h3c_ctx* ctx, const h3c_comm_id* id, int nranks, int ra
   auto* st = new h3c_comm_state();
   ncclResult_t_ r;
   int ver = 0;
-  if (n->CommInitRankConfig && n->CommGetAsyncError && n->CommAbort && n->GetVersion && n->GetVersion(&ver) == 0 &&
-      ver >= 21400) {
+  // H3C_NCCL_BLOCKING=1 keeps a blocking communicator (no abort on timeout)
+  const char* blk = getenv("H3C_NCCL_BLOCKING");
+  const bool want_blocking = blk && atoi(blk) != 0;
+  if (!want_blocking && n->CommInitRankConfig && n->CommGetAsyncError && n->CommAbort && n->GetVersion &&
+      n->GetVersion(&ver) == 0 && ver >= 21400) {
     NcclConfig cfg = nonblocking_config(ver);
     r = n->CommInitRankConfig(&st->comm, nranks, uid, rank, &cfg);
     st->nonblocking = true;
